@@ -1,0 +1,98 @@
+"""Sharded FP32-master AdamW with global clipping and pooled token normalisation.
+
+Semantics (reference: nanospec/shard.py:306-356):
+
+1. all-reduce the local weighted-token count ``den`` over the training ranks;
+2. ``factor = N * accumulation_steps / den`` (0 when den == 0) - gradients were
+   reduce-scattered with AVG, so this gives sum-of-gradients / global count;
+3. the optimizer's gradient is ``bf16(grad * factor)`` (rounded to the grad dtype);
+   its squared norm is all-reduced; a non-finite norm skips the update and zeroes
+   the gradients (``updated: False``);
+4. ``clip = min(1, max_norm / (norm + 1e-6))``; decoupled weight decay; Adam moments;
+   bias-corrected update of the fp32 master; ``param = master`` in the compute dtype.
+
+On CUDA, steps 3-4 are two kernels per shard (a squared-norm reduction and one
+fused update that also zeroes the gradient), and the finite check happens on the
+device: the update kernel reads the norm and skips itself when it is not finite.
+The host reads the three scalars once, at the end.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from ..ops import reference as ref
+from ..ops._ext import cuda_ops
+
+
+class AdamW:
+    def __init__(self, shards, lr=6e-4, weight_decay=0.0, betas=(0.9, 0.999), eps=1e-8,
+                 max_grad_norm=1.0):
+        self.shards = list(shards)
+        self.lr, self.weight_decay, self.betas = lr, weight_decay, tuple(betas)
+        self.eps, self.max_grad_norm, self.steps = eps, max_grad_norm, 0
+
+
+def zero_grad(optimizer):
+    for s in optimizer.shards:
+        s.grad.zero_()
+        s.grad_zero = True
+
+
+@torch.no_grad()
+def adamw_step(optimizer, local_denominator, accumulation_steps=1):
+    first = optimizer.shards[0]
+    den = local_denominator.detach().clone().float().reshape(())
+    if first.world_size > 1:
+        dist.all_reduce(den, group=first.group)
+    factor = torch.where(den > 0, first.world_size * accumulation_steps / den.clamp_min(1e-6),
+                         torch.zeros_like(den))
+    b1, b2 = optimizer.betas
+    if first.param.is_cuda:
+        return _adamw_cuda(optimizer, den, factor, b1, b2)
+    norm2 = torch.zeros_like(den)
+    for s in optimizer.shards:
+        norm2 += ref.scaled_grad(s.grad, factor).square().sum()
+    if first.world_size > 1:
+        dist.all_reduce(norm2, group=first.group)
+    norm = norm2.sqrt()
+    if not torch.isfinite(norm).item():
+        zero_grad(optimizer)
+        return {"grad_norm": float(norm), "updated": False, "denominator": float(den)}
+    clip = (optimizer.max_grad_norm / (norm + 1e-6)).clamp(max=1.0)
+    optimizer.steps += 1
+    for s in optimizer.shards:
+        ref.adamw_update(s.master, s.m, s.v, s.grad, factor, clip, optimizer.lr,
+                         optimizer.weight_decay, b1, b2, optimizer.eps, optimizer.steps)
+        s.param.copy_(s.master)
+    zero_grad(optimizer)
+    return {"grad_norm": float(norm), "updated": True, "denominator": float(den)}
+
+
+def _adamw_cuda(optimizer, den, factor, b1, b2):
+    C = cuda_ops()
+    first = optimizer.shards[0]
+    # norm2 and the update both consume factor from device memory: no host sync.
+    norm2 = torch.zeros(1, device=den.device, dtype=torch.float32)
+    f = factor.reshape(1).contiguous()
+    for s in optimizer.shards:
+        C.grad_norm_sq(s.grad, f, norm2)
+    if first.world_size > 1:
+        dist.all_reduce(norm2, group=first.group)
+    step = optimizer.steps + 1
+    bc1 = 1.0 - b1 ** step
+    bc2 = math.sqrt(1.0 - b2 ** step)
+    for s in optimizer.shards:
+        C.adamw_update(s.param, s.master, s.m, s.v, s.grad, f, norm2, float(optimizer.lr),
+                       float(optimizer.weight_decay), float(b1), float(b2), float(optimizer.eps),
+                       float(bc1), float(bc2), float(optimizer.max_grad_norm))
+        s.grad_zero = True
+    norm = norm2.sqrt()
+    vals = torch.stack((norm.reshape(()), den.reshape(()))).tolist()
+    finite = math.isfinite(vals[0])
+    if finite:
+        optimizer.steps = step
+    return {"grad_norm": vals[0], "updated": finite, "denominator": vals[1]}
