@@ -1,0 +1,62 @@
+// Python bindings of the sm_100a extension nanospec_b200._C.
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "common.h"
+
+namespace ns {
+void linear(at::Tensor x, at::Tensor w, at::Tensor out, c10::optional<at::Tensor> residual);
+void linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor out, bool accumulate);
+void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate);
+void gemm_test(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int splits);
+void rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, at::Tensor y, at::Tensor inv);
+void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor inv, at::Tensor w, at::Tensor dx, at::Tensor dw,
+                  c10::optional<at::Tensor> res);
+void head_norm_rope_fwd(at::Tensor x, at::Tensor w, double eps, at::Tensor cs, at::Tensor sn, at::Tensor y,
+                        at::Tensor inv);
+void head_norm_rope_bwd(at::Tensor dy, at::Tensor x, at::Tensor inv, at::Tensor w, at::Tensor cs, at::Tensor sn,
+                        at::Tensor dx, at::Tensor dw);
+void swiglu_fwd(at::Tensor gu, at::Tensor out);
+void swiglu_bwd(at::Tensor dp, at::Tensor gu, at::Tensor dgu);
+void embedding_fwd(at::Tensor ids, at::Tensor w, at::Tensor out);
+void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad);
+void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2);
+void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
+                  at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
+                  double bc1, double bc2, double max_norm);
+void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
+              at::Tensor out, at::Tensor lse);
+void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
+              at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs, at::Tensor dq, at::Tensor dk,
+              at::Tensor dv);
+std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head, c10::optional<at::Tensor> e,
+                                  c10::optional<at::Tensor> w2, c10::optional<at::Tensor> target_logits,
+                                  at::Tensor labels, at::Tensor weights, double ce_w, double kl_w,
+                                  double inv_accum, c10::optional<at::Tensor> dw2_out, int64_t chunk);
+int64_t device_error();
+void clear_device_error();
+}  // namespace ns
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nanospec_b200 sm_100a kernels";
+  m.def("linear", &ns::linear);
+  m.def("linear_dgrad", &ns::linear_dgrad);
+  m.def("linear_wgrad", &ns::linear_wgrad);
+  m.def("gemm_test", &ns::gemm_test);
+  m.def("rms_norm_fwd", &ns::rms_norm_fwd);
+  m.def("rms_norm_bwd", &ns::rms_norm_bwd);
+  m.def("head_norm_rope_fwd", &ns::head_norm_rope_fwd);
+  m.def("head_norm_rope_bwd", &ns::head_norm_rope_bwd);
+  m.def("swiglu_fwd", &ns::swiglu_fwd);
+  m.def("swiglu_bwd", &ns::swiglu_bwd);
+  m.def("embedding_fwd", &ns::embedding_fwd);
+  m.def("embedding_bwd", &ns::embedding_bwd);
+  m.def("grad_norm_sq", &ns::grad_norm_sq);
+  m.def("adamw_update", &ns::adamw_update);
+  m.def("attn_fwd", &ns::attn_fwd);
+  m.def("attn_bwd", &ns::attn_bwd);
+  m.def("head_loss", &ns::head_loss);
+  m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
+  m.def("clear_device_error", &ns::clear_device_error);
+}

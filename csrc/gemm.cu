@@ -1,0 +1,397 @@
+// bf16 GEMM on 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
+//
+//   D[M, N] = sum_k A[m, k] * B[n, k]      (fp32 accumulation in TMEM)
+//
+// A and B are each either K-major (row-major [rows, K]) or MN-major (row-major
+// [K, rows]); that covers the forward (x W^T), input-gradient (dy W) and
+// weight-gradient (dy^T x) products of a linear layer without transposes.
+// Small token counts use "swap-AB": the weight supplies the 128-row M side and
+// the output is written transposed.
+//
+// One CTA = one 128 x BN output tile over a K range (split-K across blockIdx.z):
+//   warp 0   : one thread issues TMA loads into a STAGES-deep smem ring;
+//   warp 1   : allocates TMEM; one thread issues tcgen05.mma (K = 16 per issue)
+//              and commits each stage back to the producer;
+//   warps 2-5: epilogue, tcgen05.ld of the accumulator (each warp owns the TMEM
+//              lane quarter warp % 4), then bf16 stores with optional residual /
+//              accumulate, or fp32 partials for the deterministic split-K reduce.
+// Every mbarrier wait is bounded; a timeout sets the device error flag.
+#include "common.h"
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace ns {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+struct GemmArgs {
+  int M, N, K;
+  int kpb;      // k-blocks per split
+  int splits;
+  float* out_f32;               // fp32 output (accumulate adds), used instead of `out` when set
+  __nv_bfloat16* out;
+  int64_t out_sm, out_sn;       // element strides of out(m, n)
+  const __nv_bfloat16* res;     // optional residual, same addressing as out
+  int64_t res_sm, res_sn;
+  int accumulate;               // out = out + D
+  float* ws;                    // split-K partials
+  int ws_t;                     // partial layout: 0 -> [s][m][n], 1 -> [s][n][m]
+  int* err;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, float acc) {
+  if (a.out_f32) {
+    float* q = a.out_f32 + m * a.out_sm + n * a.out_sn;
+    *q = a.accumulate ? *q + acc : acc;
+    return;
+  }
+  float y = sm100::bf16_round(acc);
+  if (a.res) y = sm100::bf16_round(__bfloat162float(a.res[m * a.res_sm + n * a.res_sn]) + y);
+  __nv_bfloat16* p = a.out + m * a.out_sm + n * a.out_sn;
+  if (a.accumulate) y = sm100::bf16_round(__bfloat162float(*p) + y);
+  *p = __float2bfloat16(y);
+}
+
+template <int BN, bool AMN, bool BMN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                     GemmArgs args) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, split = blockIdx.z;
+  const int kb_total = (args.K + BK - 1) / BK;
+  const int kb0 = split * args.kpb;
+  const int kb1 = min(kb0 + args.kpb, kb_total);
+  const int nkb = kb1 - kb0;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    sm100::mbar_init(acc_full, 1);
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&ta);
+    sm100::tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
+        sm100::mbar_expect_tx(&full[s], C::STAGE_BYTES);
+        const int k = (kb0 + i) * BK;
+        uint8_t* a_dst = sA + s * C::A_BYTES;
+        uint8_t* b_dst = sB + s * C::B_BYTES;
+        if (!AMN) {
+          sm100::tma_load_2d(a_dst, &ta, &full[s], k, m0);
+        } else {
+          sm100::tma_load_2d(a_dst, &ta, &full[s], m0, k);
+          sm100::tma_load_2d(a_dst + 8192, &ta, &full[s], m0 + 64, k);
+        }
+        if (!BMN) {
+          sm100::tma_load_2d(b_dst, &tb, &full[s], k, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(b_dst + j * 8192, &tb, &full[s], n0 + 64 * j, k);
+        }
+        issued = i + 1;
+      }
+      // Drain: the last use of every stage must have landed before the CTA exits.
+      for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+        sm100::mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, args.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_bf16(BM, BN, AMN, BMN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!sm100::mbar_wait(&full[s], ph, args.err)) break;
+        sm100::tc_fence_after();
+        const uint32_t a_base = sm100::smem_u32(sA + s * C::A_BYTES);
+        const uint32_t b_base = sm100::smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // K-major: 16 bf16 = 32 bytes along the swizzled row; MN-major: 16 rows of 128 B.
+          const uint64_t ad = AMN ? sm100::smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                  : sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
+          const uint64_t bd = BMN ? sm100::smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                  : sm100::smem_desc_sw128(b_base + kk * 32, 0, 1024);
+          sm100::mma_bf16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        sm100::mma_commit(&empty[s]);
+      }
+      sm100::mma_commit(acc_full);
+    }
+  } else {
+    const int q = warp & 3;
+    const bool ok = sm100::mbar_wait(acc_full, 0, args.err);
+    if (ok) {
+      sm100::tc_fence_after();
+      const int m = m0 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        sm100::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+        if (m >= args.M) continue;
+        const int nb = n0 + c;
+        if (args.splits > 1) {
+          float* ws = args.ws + (int64_t)split * args.M * args.N;
+          if (!args.ws_t && nb + 32 <= args.N && (args.N % 4) == 0) {
+            float4* p = reinterpret_cast<float4*>(ws + (int64_t)m * args.N + nb);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = nb + j;
+              if (n < args.N) ws[args.ws_t ? (int64_t)n * args.M + m : (int64_t)m * args.N + n] = v[j];
+            }
+          }
+        } else if (!args.out_f32 && args.out_sn == 1 && !args.res && !args.accumulate && nb + 32 <= args.N &&
+                   (args.out_sm % 8) == 0) {
+          uint4* p = reinterpret_cast<uint4*>(args.out + m * args.out_sm + nb);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(v[8 * j + 2 * t], v[8 * j + 2 * t + 1]);
+            p[j] = *reinterpret_cast<uint4*>(h);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = nb + j;
+            if (n < args.N) store_final(args, m, n, v[j]);
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Deterministic split-K reduction (fixed split order) + the final epilogue.
+__global__ void splitk_reduce_kernel(GemmArgs a) {
+  const int64_t total = (int64_t)a.M * a.N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    float acc = 0.f;
+    for (int s = 0; s < a.splits; ++s) acc += a.ws[s * total + i];
+    int m, n;
+    if (a.ws_t) {
+      n = (int)(i / a.M);
+      m = (int)(i % a.M);
+    } else {
+      m = (int)(i / a.N);
+      n = (int)(i % a.N);
+    }
+    store_final(a, m, n, acc);
+  }
+}
+
+template <int BN, bool AMN, bool BMN>
+static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid) {
+  using C = GemmCfg<BN>;
+  auto kern = gemm_bf16_kernel<BN, AMN, BMN>;
+  static bool attr = false;
+  if (!attr) {
+    NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr = true;
+  }
+  kern<<<grid, 192, C::SMEM, stream()>>>(ta, tb, a);
+  NS_CUDA(cudaGetLastError());
+}
+
+template <bool AMN, bool BMN>
+static void launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid) {
+  switch (bn) {
+    case 64: launch_bn<64, AMN, BMN>(ta, tb, a, grid); break;
+    case 128: launch_bn<128, AMN, BMN>(ta, tb, a, grid); break;
+    case 192: launch_bn<192, AMN, BMN>(ta, tb, a, grid); break;
+    default: launch_bn<256, AMN, BMN>(ta, tb, a, grid); break;
+  }
+}
+
+static int pick_bn(int N) {
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  if (N <= 192) return 192;
+  return 256;
+}
+
+// D[M,N] = A * B^T with the epilogue `e`.
+void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e,
+                 int force_splits) {
+  NS_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  const int bn = pick_bn(N);
+  CUtensorMap ta = A.mn_major ? make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BK, 64)
+                              : make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BM, 64);
+  CUtensorMap tb = B.mn_major ? make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, BK, 64)
+                              : make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, bn, 64);
+  const int mt = (M + BM - 1) / BM, nt = (N + bn - 1) / bn;
+  const int kb = (K + BK - 1) / BK;
+  const int tiles = mt * nt;
+  int splits = 1;
+  if (force_splits > 0) {
+    splits = force_splits;
+  } else if (tiles < num_sms()) {
+    splits = (num_sms() + tiles - 1) / tiles;
+    splits = std::min(splits, std::max(1, kb / 4));
+  }
+  int kpb = (kb + splits - 1) / splits;
+  splits = (kb + kpb - 1) / kpb;
+
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.kpb = kpb;
+  a.splits = splits;
+  a.out = e.out;
+  a.out_f32 = e.out_f32;
+  a.out_sm = e.sm;
+  a.out_sn = e.sn;
+  a.res = e.res;
+  a.res_sm = e.rsm;
+  a.res_sn = e.rsn;
+  a.accumulate = e.accumulate ? 1 : 0;
+  a.err = device_error_flag();
+  a.ws_t = (e.sn != 1) ? 1 : 0;
+  at::Tensor ws;
+  if (splits > 1) {
+    ws = at::empty({(int64_t)splits * M * N}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA));
+    a.ws = ws.data_ptr<float>();
+  }
+  dim3 grid(mt, nt, splits);
+  if (!A.mn_major && !B.mn_major) launch<false, false>(bn, ta, tb, a, grid);
+  else if (A.mn_major && !B.mn_major) launch<true, false>(bn, ta, tb, a, grid);
+  else if (!A.mn_major && B.mn_major) launch<false, true>(bn, ta, tb, a, grid);
+  else launch<true, true>(bn, ta, tb, a, grid);
+  if (splits > 1) {
+    const int64_t total = (int64_t)M * N;
+    int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+    splitk_reduce_kernel<<<blocks, 256, 0, stream()>>>(a);
+    NS_CUDA(cudaGetLastError());
+  }
+}
+
+// ----------------------------------------------------------------------------- torch API
+static void check_rowmajor(const at::Tensor& t, const char* name) {
+  check_bf16(t, name);
+  NS_CHECK(t.dim() == 2 && t.stride(1) == 1, std::string(name) + " must be 2-D with unit column stride");
+}
+
+// y[T, Nout] = x[T, K] @ w[Nout, K]^T (+ residual)
+void linear(at::Tensor x, at::Tensor w, at::Tensor out, c10::optional<at::Tensor> residual) {
+  check_rowmajor(x, "x");
+  check_rowmajor(w, "w");
+  check_rowmajor(out, "out");
+  const int T = x.size(0), K = x.size(1), Nout = w.size(0);
+  NS_CHECK(w.size(1) == K && out.size(0) == T && out.size(1) == Nout, "linear: shape mismatch");
+  const __nv_bfloat16* res = nullptr;
+  int64_t rs0 = 0;
+  if (residual && residual->defined()) {
+    check_rowmajor(*residual, "residual");
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    rs0 = residual->stride(0);
+  }
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  Operand X{x.data_ptr(), T, K, x.stride(0), false};
+  Operand W{w.data_ptr(), Nout, K, w.stride(0), false};
+  if (T <= 256) {
+    // swap-AB: weight rows on the 128-wide M side, tokens on N; output transposed.
+    gemm_launch(W, X, Nout, T, K, Epilogue{o, nullptr, 1, out.stride(0), res, 1, rs0, false});
+  } else {
+    gemm_launch(X, W, T, Nout, K, Epilogue{o, nullptr, out.stride(0), 1, res, rs0, 1, false});
+  }
+}
+
+// dx[T, K] (+)= dy[T, Nout] @ w[Nout, K]
+void linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor out, bool accumulate) {
+  check_rowmajor(dy, "dy");
+  check_rowmajor(w, "w");
+  check_rowmajor(out, "out");
+  const int T = dy.size(0), Nout = dy.size(1), K = w.size(1);
+  NS_CHECK(w.size(0) == Nout && out.size(0) == T && out.size(1) == K, "linear_dgrad: shape mismatch");
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (T <= 256) {
+    Operand A{w.data_ptr(), Nout, K, w.stride(0), true};    // A[m=k, r=nout] = w[nout, k]
+    Operand B{dy.data_ptr(), T, Nout, dy.stride(0), false};  // B[n=t, r=nout]
+    gemm_launch(A, B, K, T, Nout, Epilogue{o, nullptr, 1, out.stride(0), nullptr, 0, 0, accumulate});
+  } else {
+    Operand A{dy.data_ptr(), T, Nout, dy.stride(0), false};
+    Operand B{w.data_ptr(), Nout, K, w.stride(0), true};     // B[n=k, r=nout] = w[nout, k]
+    gemm_launch(A, B, T, K, Nout, Epilogue{o, nullptr, out.stride(0), 1, nullptr, 0, 0, accumulate});
+  }
+}
+
+// dW[Nout, K] (+)= dy[T, Nout]^T @ x[T, K]
+void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate) {
+  check_rowmajor(dy, "dy");
+  check_rowmajor(x, "x");
+  check_bf16(out, "out");
+  NS_CHECK(out.is_contiguous() || (out.dim() == 2 && out.stride(1) == 1), "out must be row-major");
+  const int T = dy.size(0), Nout = dy.size(1), K = x.size(1);
+  NS_CHECK(x.size(0) == T && out.numel() == (int64_t)Nout * K, "linear_wgrad: shape mismatch");
+  const int64_t ld = out.dim() == 2 ? out.stride(0) : K;
+  Operand A{dy.data_ptr(), T, Nout, dy.stride(0), true};  // A[m=nout, r=t] = dy[t, nout]
+  Operand B{x.data_ptr(), T, K, x.stride(0), true};       // B[n=k, r=t] = x[t, k]
+  gemm_launch(A, B, Nout, K, T,
+              Epilogue{reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr, ld, 1, nullptr, 0, 0, accumulate});
+}
+
+// Test hook: plain D = A * B^T with explicit operand majors and a forced split count.
+void gemm_test(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int splits) {
+  check_rowmajor(a, "a");
+  check_rowmajor(b, "b");
+  check_rowmajor(out, "out");
+  const int M = out.size(0), N = out.size(1);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  Operand A{a.data_ptr(), a.size(0), a.size(1), a.stride(0), a_mn};
+  Operand B{b.data_ptr(), b.size(0), b.size(1), b.stride(0), b_mn};
+  gemm_launch(A, B, M, N, K,
+              Epilogue{reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr, out.stride(0), 1, nullptr, 0, 0, false},
+              splits);
+}
+
+}  // namespace ns

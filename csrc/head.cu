@@ -1,0 +1,270 @@
+// LM head + Markov head + 0.1 CE + 0.9 KL(target || draft), forward and backward,
+// streamed over the vocabulary in chunks so the [tokens, vocab] logits are never
+// materialised (only one [2T, Vc] chunk lives in a scratch buffer).
+//
+// pass 1, per chunk c (vocab [v0, v0 + Vc)):
+//   L[0:T]  = bf16(h W_c^T) ; L[0:T] = bf16(L + bf16(E1[prev] W2_c^T))   (draft logits)
+//   L[T:2T] = bf16(h_t W_c^T)                                           (target logits)
+//   stats  : per (row, chunk-part) max / sum-exp of draft and target logits, the
+//            target-weighted logit gap sum_v exp(t - m) (t - l), and the label logit.
+// merge    : lse_draft, lse_target, CE (bf16-rounded like F.cross_entropy on bf16
+//            logits) and KL per token.
+// pass 2, per chunk: recompute L, then the logits gradient (CE at the bf16 boundary,
+//            KL in fp32), sum_v min(p, q) partials, and
+//            dh (fp32) += dl W_c, de (fp32) += dl W2_c, dW2_c = dl^T E1[prev].
+// All reductions use fixed-order partial buffers: results are run-to-run identical.
+#include "common.h"
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace ns {
+
+using bf16 = __nv_bfloat16;
+constexpr int VPARTS = 4;  // blocks per row per chunk in the stats / grad kernels
+
+struct Stat {
+  float ml, zl, mt, zt, s1;
+};
+
+__device__ __forceinline__ void merge(Stat& a, const Stat& b) {
+  // draft
+  float m = fmaxf(a.ml, b.ml);
+  float za = (a.ml == -INFINITY) ? 0.f : a.zl * expf(a.ml - m);
+  float zb = (b.ml == -INFINITY) ? 0.f : b.zl * expf(b.ml - m);
+  a.ml = m;
+  a.zl = za + zb;
+  // target (s1 scales with the target max)
+  m = fmaxf(a.mt, b.mt);
+  const float fa = (a.mt == -INFINITY) ? 0.f : expf(a.mt - m);
+  const float fb = (b.mt == -INFINITY) ? 0.f : expf(b.mt - m);
+  a.mt = m;
+  a.zt = a.zt * fa + b.zt * fb;
+  a.s1 = a.s1 * fa + b.s1 * fb;
+}
+
+// grid (T, VPARTS): block (t, p) scans columns [p*Vc/VPARTS, ...) of the chunk.
+__global__ void head_stats_kernel(const bf16* __restrict__ L, int64_t ldl, const bf16* __restrict__ Tt,
+                                  int64_t ldt, int vc, int v0, const int64_t* __restrict__ labels,
+                                  Stat* __restrict__ part, float* __restrict__ label_logit, int chunk, int T) {
+  const int t = blockIdx.x, p = blockIdx.y;
+  const int per = (vc + VPARTS - 1) / VPARTS;
+  const int c0 = p * per, c1 = min(vc, c0 + per);
+  const bf16* lr = L + (int64_t)t * ldl;
+  const bf16* tr = Tt + (int64_t)t * ldt;
+  Stat s{-INFINITY, 0.f, -INFINITY, 0.f, 0.f};
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+    const float l = __bfloat162float(lr[c]);
+    const float tv = __bfloat162float(tr[c]);
+    Stat o{l, 1.f, tv, 1.f, tv - l};
+    merge(s, o);
+  }
+  // block reduction in fixed order (warp shuffles, then warp 0)
+  __shared__ Stat sh[32];
+  for (int off = 16; off > 0; off >>= 1) {
+    Stat o;
+    o.ml = __shfl_xor_sync(0xffffffff, s.ml, off);
+    o.zl = __shfl_xor_sync(0xffffffff, s.zl, off);
+    o.mt = __shfl_xor_sync(0xffffffff, s.mt, off);
+    o.zt = __shfl_xor_sync(0xffffffff, s.zt, off);
+    o.s1 = __shfl_xor_sync(0xffffffff, s.s1, off);
+    merge(s, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Stat a = sh[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) merge(a, sh[i]);
+    part[((int64_t)chunk * VPARTS + p) * T + t] = a;
+    const int64_t lab = labels[t];
+    if (lab >= v0 + c0 && lab < v0 + c1) label_logit[t] = __bfloat162float(lr[lab - v0]);
+  }
+}
+
+// Per row: merge all partials; write lse_l, lse_t, ce (bf16-rounded), kl.
+__global__ void head_merge_kernel(const Stat* __restrict__ part, int nparts, int T,
+                                  const float* __restrict__ label_logit, float* __restrict__ row) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  Stat a{-INFINITY, 0.f, -INFINITY, 0.f, 0.f};
+  for (int i = 0; i < nparts; ++i) merge(a, part[(int64_t)i * T + t]);
+  const float lse_l = a.ml + logf(a.zl);
+  const float lse_t = a.mt + logf(a.zt);
+  const float ce = sm100::bf16_round(lse_l - label_logit[t]);
+  const float kl = a.s1 / a.zt - lse_t + lse_l;
+  row[t * 6 + 0] = ce;
+  row[t * 6 + 1] = kl;
+  row[t * 6 + 3] = lse_l;
+  row[t * 6 + 4] = lse_t;
+}
+
+// Pass-2 elementwise: dl and sum_v min(p, q) partials.
+__global__ void head_grad_kernel(const bf16* __restrict__ L, int64_t ldl, const bf16* __restrict__ Tt,
+                                 int64_t ldt, int vc, int v0, const int64_t* __restrict__ labels,
+                                 const float* __restrict__ weights, const float* __restrict__ row, float ce_w,
+                                 float kl_w, float inv_accum, bf16* __restrict__ dl, int64_t lddl,
+                                 float* __restrict__ minpart, int chunk, int T) {
+  const int t = blockIdx.x, p = blockIdx.y;
+  const int per = (vc + VPARTS - 1) / VPARTS;
+  const int c0 = p * per, c1 = min(vc, c0 + per);
+  const float lse_l = row[t * 6 + 3], lse_t = row[t * 6 + 4];
+  const float scale = weights[t] * inv_accum;
+  const float ce_s = sm100::bf16_round(scale * ce_w);
+  const float kl_s = scale * kl_w;
+  const int64_t lab = labels[t];
+  const bf16* lr = L + (int64_t)t * ldl;
+  const bf16* tr = Tt + (int64_t)t * ldt;
+  bf16* dr = dl + (int64_t)t * lddl;
+  float mn = 0.f;
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+    const float l = __bfloat162float(lr[c]);
+    const float tv = __bfloat162float(tr[c]);
+    const float pd = expf(l - lse_l);
+    const float pt = expf(tv - lse_t);
+    mn += fminf(pd, pt);
+    // CE part at the compute-dtype boundary: bf16(exp(bf16(log_softmax))) * bf16(scale)
+    const float ls = sm100::bf16_round(l - lse_l);
+    float dce = sm100::bf16_round(sm100::bf16_round(expf(ls)) * ce_s);
+    if (v0 + c == lab) dce = sm100::bf16_round(dce - ce_s);
+    const float dkl = sm100::bf16_round((pd - pt) * kl_s);
+    dr[c] = __float2bfloat16(dce + dkl);
+  }
+  __shared__ float sh[32];
+  for (int off = 16; off > 0; off >>= 1) mn += __shfl_xor_sync(0xffffffff, mn, off);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = mn;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += sh[i];
+    minpart[((int64_t)chunk * VPARTS + p) * T + t] = s;
+  }
+}
+
+__global__ void head_min_merge_kernel(const float* __restrict__ minpart, int nparts, int T, float* __restrict__ row) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float s = 0.f;
+  for (int i = 0; i < nparts; ++i) s += minpart[(int64_t)i * T + t];
+  row[t * 6 + 2] = s;
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, bf16* __restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16(in[i]);
+}
+
+// ----------------------------------------------------------------------------- host
+// hcat: [T or 2T, H] = [draft hidden ; target hidden] (target rows absent when
+// target_logits is given). Returns per-row stats [T, 6] =
+// (ce, kl, sum_v min(p,q), lse_draft, lse_target, unused); writes dh [T, H], de [T, r], dW2.
+std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head, c10::optional<at::Tensor> e,
+                                  c10::optional<at::Tensor> w2, c10::optional<at::Tensor> target_logits,
+                                  at::Tensor labels, at::Tensor weights, double ce_w, double kl_w,
+                                  double inv_accum, c10::optional<at::Tensor> dw2_out, int64_t chunk) {
+  check_bf16(hcat, "hcat");
+  check_bf16(lm_head, "lm_head");
+  NS_CHECK(hcat.is_contiguous() && lm_head.is_contiguous(), "head: contiguous inputs expected");
+  const int64_t V = lm_head.size(0), H = lm_head.size(1);
+  const bool markov = e.has_value() && e->defined();
+  const bool tl = target_logits.has_value() && target_logits->defined();
+  NS_CHECK(hcat.size(0) == (tl ? T : 2 * T), "hcat rows must be T (teacher logits) or 2T");
+  NS_CHECK(labels.scalar_type() == at::kLong && labels.numel() == T, "labels [T] int64");
+  NS_CHECK(weights.scalar_type() == at::kFloat && weights.numel() == T, "weights [T] fp32");
+  auto opt = hcat.options();
+  const int64_t vc = std::min<int64_t>(chunk, V);
+  const int nchunks = (int)((V + vc - 1) / vc);
+  const int64_t R = hcat.size(0);
+  auto Lbuf = at::empty({R, vc}, opt);
+  auto dl = at::empty({T, vc}, opt);
+  auto part = at::empty({(int64_t)nchunks * VPARTS * T * 5}, opt.dtype(at::kFloat));
+  auto minpart = at::empty({(int64_t)nchunks * VPARTS * T}, opt.dtype(at::kFloat));
+  auto label_logit = at::zeros({T}, opt.dtype(at::kFloat));
+  auto row = at::zeros({T, 6}, opt.dtype(at::kFloat));
+  auto dh32 = at::zeros({T, H}, opt.dtype(at::kFloat));
+  int64_t r = markov ? e->size(1) : 0;
+  auto de32 = markov ? at::zeros({T, r}, opt.dtype(at::kFloat)) : at::Tensor();
+  const int64_t* lab = labels.data_ptr<int64_t>();
+  auto* Lp = reinterpret_cast<bf16*>(Lbuf.data_ptr());
+  Stat* partp = reinterpret_cast<Stat*>(part.data_ptr<float>());
+
+  auto logits_chunk = [&](int64_t v0, int64_t n) {
+    // L[0:R, 0:n] = hcat W_c^T   (swap-AB: vocab rows on M, tokens on N)
+    Operand W{lm_head.data_ptr<at::BFloat16>() + v0 * H, n, H, H, false};
+    Operand X{hcat.data_ptr(), R, H, H, false};
+    gemm_launch(W, X, (int)n, (int)R, (int)H, Epilogue{Lp, nullptr, 1, vc, nullptr, 0, 0, false});
+    if (markov) {
+      Operand W2{w2->data_ptr<at::BFloat16>() + v0 * r, n, r, r, false};
+      Operand E{e->data_ptr(), T, r, r, false};
+      gemm_launch(W2, E, (int)n, (int)T, (int)r, Epilogue{Lp, nullptr, 1, vc, nullptr, 0, 0, true});
+    }
+  };
+  auto target_ptr = [&](int64_t v0, int64_t& ld) -> const bf16* {
+    if (tl) {
+      ld = target_logits->stride(0);
+      return reinterpret_cast<const bf16*>(target_logits->data_ptr()) + v0;
+    }
+    ld = vc;
+    return Lp + T * vc;
+  };
+
+  // ---------------- pass 1
+  for (int c = 0; c < nchunks; ++c) {
+    const int64_t v0 = c * vc, n = std::min(vc, V - v0);
+    logits_chunk(v0, n);
+    int64_t ldt;
+    const bf16* tp = target_ptr(v0, ldt);
+    head_stats_kernel<<<dim3(T, VPARTS), 256, 0, stream()>>>(Lp, vc, tp, ldt, (int)n, (int)v0, lab, partp,
+                                                            label_logit.data_ptr<float>(), c, (int)T);
+    NS_CUDA(cudaGetLastError());
+  }
+  head_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(partp, nchunks * VPARTS, (int)T,
+                                                           label_logit.data_ptr<float>(), row.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+
+  // ---------------- pass 2
+  auto* dlp = reinterpret_cast<bf16*>(dl.data_ptr());
+  for (int c = 0; c < nchunks; ++c) {
+    const int64_t v0 = c * vc, n = std::min(vc, V - v0);
+    logits_chunk(v0, n);
+    int64_t ldt;
+    const bf16* tp = target_ptr(v0, ldt);
+    head_grad_kernel<<<dim3(T, VPARTS), 256, 0, stream()>>>(
+        Lp, vc, tp, ldt, (int)n, (int)v0, lab, weights.data_ptr<float>(), row.data_ptr<float>(), (float)ce_w,
+        (float)kl_w, (float)inv_accum, dlp, vc, minpart.data_ptr<float>(), c, (int)T);
+    NS_CUDA(cudaGetLastError());
+    // dh[T, H] += dl[T, n] W_c[n, H]   (swap-AB: H on M, tokens on N, reduce over vocab)
+    {
+      Operand A{lm_head.data_ptr<at::BFloat16>() + v0 * H, n, H, H, true};
+      Operand B{dlp, T, n, vc, false};
+      gemm_launch(A, B, (int)H, (int)T, (int)n, Epilogue{nullptr, dh32.data_ptr<float>(), 1, H, nullptr, 0, 0, c > 0});
+    }
+    if (markov) {
+      Operand A{w2->data_ptr<at::BFloat16>() + v0 * r, n, r, r, true};
+      Operand B{dlp, T, n, vc, false};
+      gemm_launch(A, B, (int)r, (int)T, (int)n, Epilogue{nullptr, de32.data_ptr<float>(), 1, r, nullptr, 0, 0, c > 0});
+      // dW2[v0:v0+n, r] = dl^T E1[prev]
+      Operand DA{dlp, T, n, vc, true};
+      Operand EB{e->data_ptr(), T, r, r, true};
+      gemm_launch(DA, EB, (int)n, (int)r, (int)T,
+                  Epilogue{reinterpret_cast<bf16*>(dw2_out->data_ptr()) + v0 * r, nullptr, r, 1, nullptr, 0, 0, false});
+    }
+  }
+  head_min_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(minpart.data_ptr<float>(), nchunks * VPARTS, (int)T,
+                                                               row.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+  auto dh = at::empty({T, H}, opt);
+  f32_to_bf16_kernel<<<num_sms() * 4, 256, 0, stream()>>>(dh32.data_ptr<float>(), reinterpret_cast<bf16*>(dh.data_ptr()),
+                                                          T * H);
+  NS_CUDA(cudaGetLastError());
+  at::Tensor de;
+  if (markov) {
+    de = at::empty({T, r}, opt);
+    f32_to_bf16_kernel<<<num_sms(), 256, 0, stream()>>>(de32.data_ptr<float>(), reinterpret_cast<bf16*>(de.data_ptr()),
+                                                        T * r);
+    NS_CUDA(cudaGetLastError());
+  }
+  return {row, dh, de};
+}
+
+}  // namespace ns

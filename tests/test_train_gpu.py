@@ -1,0 +1,73 @@
+"""End-to-end train() on the GPU (CUDA kernels) vs the CPU path of the same model."""
+
+import pytest
+import torch
+
+import nanospec_b200 as N
+
+pytestmark = pytest.mark.gpu
+cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+
+
+def _model(c, dev, dtype):
+    g = torch.Generator().manual_seed(43)
+    emb = (torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1).to(dtype)
+    head = (torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1).to(dtype)
+    return N.DSpark(c, N.initialize(c, 42, dtype), emb, head, device=dev, dtype=dtype)
+
+
+@cuda
+@pytest.mark.parametrize("name,seq,batch", [("tiny", 128, 1), ("tiny-hybrid", 128, 1), ("tiny", 96, 2)])
+def test_train_step_gpu_matches_cpu(name, seq, batch):
+    c = N.DraftConfig.load(N.config_path(name))
+    o = N.Objective(num_anchors=8)
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, c.vocab_size, (batch, seq), generator=g)
+    hs = [torch.randn(batch, seq, c.hidden_size, generator=g).to(dtype) for _ in range(c.num_target_layers)]
+    last = torch.randn(batch, seq, c.hidden_size, generator=g).to(dtype)
+    mask = torch.ones(batch, seq)
+    mask[:, 40:42] = 0
+    res = {}
+    for dev in ("cpu", "cuda"):
+        m = _model(c, dev, dtype)
+        opt = N.AdamW(m.sharding, lr=1e-3, weight_decay=0.01)
+        torch.manual_seed(0)
+        anchors = N.sample_anchors(ids, mask, o)
+        to = lambda t: t.to(dev)  # noqa: E731
+        losses = []
+        for _ in range(2):
+            r = N.train(to(ids), m, o, teacher_batch=N.TeacherBatch([to(h) for h in hs], to(last)),
+                        loss_mask=to(mask), anchors=(to(anchors[0]), to(anchors[1])), optimizer=None)
+            grads = [s.grad.float().cpu().clone() for s in m.sharding]
+            u = N.adamw_step(opt, r.metrics.denominator)
+            losses.append((r.metrics.loss.item(), r.metrics.accept_len.item(), u["grad_norm"]))
+        res[dev] = (losses, grads, [s.master.cpu().clone() for s in m.sharding])
+    (lc, gc, mc), (lg, gg, mg) = res["cpu"], res["cuda"]
+    for a, b in zip(lc, lg):
+        assert abs(a[0] - b[0]) / abs(a[0]) < 0.02
+        assert abs(a[1] - b[1]) < 0.05
+        assert abs(a[2] - b[2]) / a[2] < 0.05
+    for a, b in zip(gc, gg):
+        cos = torch.nn.functional.cosine_similarity(a, b, dim=0).item()
+        assert cos > 0.99, cos
+    for a, b in zip(mc, mg):
+        assert ((a - b).norm() / a.norm()).item() < 3e-3
+
+
+@cuda
+def test_train_step_deterministic():
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    o = N.Objective(num_anchors=8)
+    ids = torch.randint(0, c.vocab_size, (1, 128), device="cuda")
+    hs = [torch.randn(1, 128, c.hidden_size, device="cuda").bfloat16() for _ in range(2)]
+    last = torch.randn(1, 128, c.hidden_size, device="cuda").bfloat16()
+    out = []
+    for _ in range(2):
+        m = _model(c, "cuda", torch.bfloat16)
+        torch.manual_seed(3)
+        r = N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last))
+        out.append(([s.grad.clone() for s in m.sharding], r.hidden.clone()))
+    for a, b in zip(out[0][0], out[1][0]):
+        assert torch.equal(a, b)
+    assert torch.equal(out[0][1], out[1][1])
