@@ -34,6 +34,16 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
                                   c10::optional<at::Tensor> w2, c10::optional<at::Tensor> target_logits,
                                   at::Tensor labels, at::Tensor weights, double ce_w, double kl_w,
                                   double inv_accum, c10::optional<at::Tensor> dw2_out, int64_t chunk);
+void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out);
+void add_bf16(at::Tensor a, at::Tensor b, at::Tensor o);
+void silu_mul(at::Tensor g, at::Tensor u, at::Tensor o);
+void qwen_norm(at::Tensor x, at::Tensor w, double eps, at::Tensor y);
+void gated_norm(at::Tensor x, at::Tensor gate, at::Tensor w, double eps, at::Tensor y);
+void conv_silu(at::Tensor x, at::Tensor w, at::Tensor y);
+void gdn_gates(at::Tensor a, at::Tensor b, at::Tensor alog, at::Tensor dtb, at::Tensor g, at::Tensor beta);
+void gdn_chunk_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, int64_t groups, at::Tensor out);
+void causal_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor gate, at::Tensor cs, at::Tensor sn, int64_t rd,
+                     at::Tensor out);
 int64_t device_error();
 void clear_device_error();
 }  // namespace ns
@@ -57,6 +67,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &ns::attn_fwd);
   m.def("attn_bwd", &ns::attn_bwd);
   m.def("head_loss", &ns::head_loss);
+  m.def("fp8_linear", &ns::fp8_linear);
+  m.def("add_bf16", &ns::add_bf16);
+  m.def("silu_mul", &ns::silu_mul);
+  m.def("qwen_norm", &ns::qwen_norm);
+  m.def("gated_norm", &ns::gated_norm);
+  m.def("conv_silu", &ns::conv_silu);
+  m.def("gdn_gates", &ns::gdn_gates);
+  m.def("gdn_chunk_fwd", &ns::gdn_chunk_fwd);
+  m.def("causal_attn_fwd", &ns::causal_attn_fwd);
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
   m.def("clear_device_error", &ns::clear_device_error);
 }

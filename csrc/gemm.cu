@@ -67,16 +67,16 @@ __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, flo
 template <int BN, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     GemmArgs args) {
+                     GemmArgs args, int stages) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* acc_full = empty + C::STAGES;
+  uint8_t* sB = smem + stages * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * C::B_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(192, 1)
   const int nkb = kb1 - kb0;
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
@@ -109,9 +109,9 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
+        if (i >= stages && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
         sm100::mbar_expect_tx(&full[s], C::STAGE_BYTES);
         const int k = (kb0 + i) * BK;
         uint8_t* a_dst = sA + s * C::A_BYTES;
@@ -131,15 +131,15 @@ __global__ void __launch_bounds__(192, 1)
         issued = i + 1;
       }
       // Drain: the last use of every stage must have landed before the CTA exits.
-      for (int i = max(0, issued - C::STAGES); i < issued; ++i)
-        sm100::mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, args.err);
+      for (int i = max(0, issued - stages); i < issued; ++i)
+        sm100::mbar_wait(&full[i % stages], (i / stages) & 1, args.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = sm100::idesc_bf16(BM, BN, AMN, BMN);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
         if (!sm100::mbar_wait(&full[s], ph, args.err)) break;
         sm100::tc_fence_after();
         const uint32_t a_base = sm100::smem_u32(sA + s * C::A_BYTES);
@@ -238,7 +238,12 @@ static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr = true;
   }
-  kern<<<grid, 192, C::SMEM, stream()>>>(ta, tb, a);
+  // A CTA never needs more ring stages than it has k-blocks; a short K (weight
+  // gradients over a few dozen tokens) then uses little shared memory and several
+  // CTAs share an SM, overlapping one CTA's epilogue with another's loads.
+  const int stages = std::max(1, std::min(C::STAGES, a.kpb));
+  const int smem = stages * C::STAGE_BYTES + 1024 + 256;
+  kern<<<grid, 192, smem, stream()>>>(ta, tb, a, stages);
   NS_CUDA(cudaGetLastError());
 }
 

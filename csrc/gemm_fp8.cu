@@ -1,0 +1,264 @@
+// Block-scaled FP8 projection for the frozen verifier on tcgen05 (kind::f8f6f4).
+//
+//   y[t, n] = sum_kb  sa[t, kb] * sb[n/128, kb] * sum_{k in block kb} qa[t, k] qb[n, k]
+//
+// qa/sa: activations quantised per token per 128 channels (e4m3, scale = amax/448);
+// qb/sb: e4m3 weights with one fp32 scale per 128 x 128 block (weight_scale_inv).
+// The scales are arbitrary fp32 (not powers of two), so they cannot be folded into
+// the MMA as microscaling factors. Instead each 128-wide K block is accumulated by
+// the tensor cores into its own TMEM buffer (two buffers alternate), and the
+// epilogue warps promote it: acc += sa * sb * partial, in fp32 registers, while the
+// tensor cores already work on the next K block.
+//
+// CTA: 128 tokens x 128 output channels. warp 0: TMA producer; warp 1: TMEM owner +
+// MMA issuer; warps 2-5: promotion/epilogue (TMEM lane quarter = warp % 4).
+#include "common.h"
+#include "sm100.cuh"
+
+#include <cuda_fp8.h>
+
+namespace ns {
+
+constexpr int F8_BM = 128, F8_BN = 128, F8_BK = 128;
+constexpr int F8_STAGE = F8_BM * F8_BK + F8_BN * F8_BK;  // bytes
+constexpr int F8_STAGES = 6;
+constexpr int F8_SMEM = F8_STAGES * F8_STAGE + 1024 + 512;
+
+// kind::f8f6f4 instruction descriptor: e4m3 x e4m3 -> f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+struct F8Args {
+  int M, N, K;
+  const float* sa;  // [M, K/128]
+  const float* sb;  // [N/128, K/128]
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int* err;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, F8Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + F8_STAGES * F8_BM * F8_BK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + F8_STAGES * F8_BN * F8_BK);
+  uint64_t* empty = full + F8_STAGES;
+  uint64_t* tfull = empty + F8_STAGES;  // [2] accumulator buffer ready
+  uint64_t* tempty = tfull + 2;         // [2] accumulator buffer drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * F8_BM, n0 = blockIdx.y * F8_BN;
+  const int nkb = (args.K + F8_BK - 1) / F8_BK;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < F8_STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 128);
+    }
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&ta);
+    sm100::tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 256);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % F8_STAGES;
+        const uint32_t ph = (i / F8_STAGES) & 1;
+        if (i >= F8_STAGES && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
+        sm100::mbar_expect_tx(&full[s], F8_STAGE);
+        sm100::tma_load_2d(sA + s * F8_BM * F8_BK, &ta, &full[s], i * F8_BK, m0);
+        sm100::tma_load_2d(sB + s * F8_BN * F8_BK, &tb, &full[s], i * F8_BK, n0);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - F8_STAGES); i < issued; ++i)
+        sm100::mbar_wait(&full[i % F8_STAGES], (i / F8_STAGES) & 1, args.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3(F8_BM, F8_BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % F8_STAGES;
+        const uint32_t ph = (i / F8_STAGES) & 1;
+        const int buf = i & 1;
+        // accumulator buffer `buf` must have been drained by the promotion warps
+        if (i >= 2 && !sm100::mbar_wait(&tempty[buf], ((i >> 1) - 1) & 1, args.err)) break;
+        if (!sm100::mbar_wait(&full[s], ph, args.err)) break;
+        sm100::tc_fence_after();
+        const uint32_t a_base = sm100::smem_u32(sA + s * F8_BM * F8_BK);
+        const uint32_t b_base = sm100::smem_u32(sB + s * F8_BN * F8_BK);
+        const uint32_t d = tmem + (uint32_t)(buf * F8_BN);
+#pragma unroll
+        for (int kk = 0; kk < F8_BK / 32; ++kk) {
+          const uint64_t ad = sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
+          const uint64_t bd = sm100::smem_desc_sw128(b_base + kk * 32, 0, 1024);
+          mma_f8(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        sm100::mma_commit(&empty[s]);
+        sm100::mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int m = m0 + row;
+    const int kbs = (args.K + 127) / 128;
+    float acc[F8_BN];
+#pragma unroll
+    for (int j = 0; j < F8_BN; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int buf = i & 1;
+      ok = sm100::mbar_wait(&tfull[buf], (i >> 1) & 1, args.err);
+      if (!ok) break;
+      sm100::tc_fence_after();
+      const float sbv = args.sb[(n0 / 128) * kbs + i];
+      const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + i] : 0.f;
+      const float f = sav * sbv;
+#pragma unroll
+      for (int c = 0; c < F8_BN; c += 32) {
+        float v[32];
+        sm100::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * F8_BN + c), v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c + j] += f * v[j];
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[buf]);
+    }
+    if (ok && m < args.M) {
+      __nv_bfloat16* o = args.out + (int64_t)m * args.ldo + n0;
+      if (n0 + F8_BN <= args.N && (args.ldo % 8) == 0) {
+        uint4* p = reinterpret_cast<uint4*>(o);
+#pragma unroll
+        for (int j = 0; j < F8_BN / 8; ++j) {
+          __nv_bfloat162 h[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[8 * j + 2 * t], acc[8 * j + 2 * t + 1]);
+          p[j] = *reinterpret_cast<uint4*>(h);
+        }
+      } else {
+        for (int j = 0; j < F8_BN; ++j)
+          if (n0 + j < args.N) o[j] = __float2bfloat16(acc[j]);
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 256);
+  }
+}
+
+// 1 x 128 dynamic activation quantisation: one warp per (token, 128-channel block).
+__global__ void quant_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int K, uint8_t* __restrict__ q,
+                                  float* __restrict__ scale) {
+  const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kbs = K / 128;
+  if (wid >= rows * kbs) return;
+  const int64_t r = wid / kbs;
+  const int kb = (int)(wid % kbs);
+  const __nv_bfloat16* src = x + r * K + kb * 128 + lane * 4;
+  float v[4];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = __bfloat162float(src[i]);
+    amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, o));
+  const float s = amax / 448.f;
+  const float denom = fmaxf(s, 1.17549435e-38f);
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float y = fminf(fmaxf(v[i] / denom, -448.f), 448.f);
+    const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+    packed |= (uint32_t)b << (8 * i);
+  }
+  *reinterpret_cast<uint32_t*>(q + r * K + kb * 128 + lane * 4) = packed;
+  if (lane == 0) scale[r * kbs + kb] = s;
+}
+
+static CUtensorMap make_tmap_u8(const void* base, int64_t rows, int64_t cols, int box_rows) {
+  NS_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  NS_CHECK(cols % 16 == 0, "fp8 rows must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  NS_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp8) failed");
+  return map;
+}
+
+// Quantise x, then the block-scaled GEMM. Also returns nothing: writes out [T, N] bf16.
+void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out) {
+  check_bf16(x, "x");
+  NS_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "fp8_linear: contiguous tensors expected");
+  NS_CHECK(w.scalar_type() == at::kFloat8_e4m3fn, "weight must be float8_e4m3fn");
+  const int64_t T = x.size(0);
+  const int K = x.size(1), N = w.size(0);
+  NS_CHECK(K % 128 == 0 && N % 128 == 0 && w.size(1) == K, "FP8 weights need 128 x 128 blocks");
+  NS_CHECK(scale_inv.scalar_type() == at::kFloat && scale_inv.size(0) == N / 128 && scale_inv.size(1) == K / 128,
+           "weight_scale_inv must be fp32 [N/128, K/128]");
+  if (T == 0) return;
+  auto q = at::empty({T, K}, x.options().dtype(at::kByte));
+  auto sa = at::empty({T, K / 128}, x.options().dtype(at::kFloat));
+  const int64_t warps = T * (K / 128);
+  quant_e4m3_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), T, K, q.data_ptr<uint8_t>(), sa.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+  CUtensorMap ta = make_tmap_u8(q.data_ptr(), T, K, F8_BM);
+  CUtensorMap tb = make_tmap_u8(w.data_ptr(), N, K, F8_BN);
+  F8Args a{};
+  a.M = (int)T;
+  a.N = N;
+  a.K = K;
+  a.sa = sa.data_ptr<float>();
+  a.sb = scale_inv.contiguous().data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = out.stride(0);
+  a.err = device_error_flag();
+  static bool attr = false;
+  if (!attr) {
+    NS_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM));
+    attr = true;
+  }
+  dim3 grid((unsigned)((T + F8_BM - 1) / F8_BM), (unsigned)(N / F8_BN));
+  fp8_gemm_kernel<<<grid, 192, F8_SMEM, stream()>>>(ta, tb, a);
+  NS_CUDA(cudaGetLastError());
+}
+
+}  // namespace ns

@@ -194,3 +194,151 @@ def adamw_update(master, m, v, grad, factor, clip, lr, wd, b1, b2, eps, step):
     v.mul_(b2).addcmul_(g, g, value=1 - b2)
     denom = v.sqrt().div_((1 - b2 ** step) ** 0.5).add_(eps)
     master.addcdiv_(m, denom, value=-lr / (1 - b1 ** step))
+
+
+# --------------------------------------------------------------------- verifier ops
+def qwen_norm(x, w, eps):
+    """Qwen3.5 RMSNorm: weight applied as (1 + w), everything in fp32, one final cast."""
+    y = x.float()
+    y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + eps)
+    return (y * (1.0 + w.float())).to(x.dtype)
+
+
+def qwen_gated_norm(x, gate, w, eps):
+    """w * bf16(rmsnorm(x)) * silu(gate) (fp32 gate), cast to x.dtype."""
+    xf = x.float()
+    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+    return (w * n * F.silu(gate.float())).to(x.dtype)
+
+
+def quantize_fp8_rows(x, block=128):
+    """Dynamic 1 x 128 e4m3 quantisation: returns (q [.., K] e4m3, scale [.., K/128] fp32)."""
+    xb = x.float().reshape(*x.shape[:-1], -1, block)
+    s = xb.abs().amax(-1, keepdim=True) / 448.0
+    q = (xb / s.clamp_min(torch.finfo(torch.float32).tiny)).clamp(-448, 448).to(torch.float8_e4m3fn)
+    return q.reshape(x.shape), s.squeeze(-1)
+
+
+def fp8_linear(x, w, scale_inv, block=128):
+    """Block-scaled FP8 projection: dequantised activations and weights, fp32 GEMM, cast.
+
+    Non-FP8 weights run a plain linear. The dequantise-then-fp32-GEMM form is the
+    numerical oracle for the tensor-core kernel.
+    """
+    if w.dtype != torch.float8_e4m3fn:
+        return F.linear(x, w)
+    n, k = w.shape
+    if n % block or k % block:
+        raise ValueError("FP8 weights need 128 x 128 blocks")
+    q, s = quantize_fp8_rows(x, block)
+    xd = (q.float().reshape(*x.shape[:-1], -1, block) * s.unsqueeze(-1)).reshape(x.shape)
+    wd = (w.float().view(n // block, block, k // block, block) * scale_inv[:, None, :, None]).reshape(n, k)
+    return F.linear(xd, wd).to(x.dtype)
+
+
+def causal_conv_silu(x, w):
+    """Depthwise causal conv1d (kernel K, left padding K-1) followed by SiLU.
+
+    x [b, s, C] (token-major), w [C, 1, K]. Returns [b, s, C] in x.dtype.
+    """
+    b, s, c = x.shape
+    kk = w.shape[-1]
+    y = F.conv1d(x.transpose(1, 2), w, padding=kk - 1, groups=c)[..., :s]
+    return F.silu(y).transpose(1, 2)
+
+
+def gdn_gates(a, b, a_log, dt_bias):
+    """g = -exp(A_log) * softplus(a + dt_bias) (fp32) and beta = sigmoid(b)."""
+    g = -a_log.float().exp() * F.softplus(a.float() + dt_bias.float())
+    return g, b.sigmoid()
+
+
+def l2norm(x, eps=1e-6):
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
+
+
+def gated_delta_rule_recurrent(q, k, v, g, beta):
+    """Token-by-token gated delta rule in fp32 (oracle).
+
+    q, k [b, s, h, dk]; v [b, s, h, dv]; g, beta [b, s, h]. q and k are L2-normalised
+    here and q is scaled by dk^-1/2. State S [dk, dv]:
+    S <- exp(g) S;  S <- S + k (beta (v - S^T k))^T;  o = S^T q.
+    """
+    dtype = q.dtype
+    q = l2norm(q.float()) * q.shape[-1] ** -0.5
+    k = l2norm(k.float())
+    v, g, beta = v.float(), g.float(), beta.float()
+    b, s, h, dk = k.shape
+    state = torch.zeros(b, h, dk, v.shape[-1], dtype=torch.float32, device=q.device)
+    out = torch.empty(b, s, h, v.shape[-1], dtype=torch.float32, device=q.device)
+    for t in range(s):
+        state = state * g[:, t].exp()[..., None, None]
+        kv = torch.einsum("bhkv,bhk->bhv", state, k[:, t])
+        delta = (v[:, t] - kv) * beta[:, t, :, None]
+        state = state + k[:, t, :, :, None] * delta[:, :, None, :]
+        out[:, t] = torch.einsum("bhkv,bhk->bhv", state, q[:, t])
+    return out.to(dtype)
+
+
+def gated_delta_rule_chunked(q, k, v, g, beta, chunk=64):
+    """Chunked (WY-form) gated delta rule; same math as the recurrence, fp32 inside.
+
+    Per chunk with in-chunk cumulative decay G: T = (I + tril(beta k k^T e^{G_i-G_j}, -1))^-1,
+    U = T (beta v), W = T (beta k e^G); then with the carried state S:
+    v' = U - W S;  o = (q e^G) S + tril(q k^T e^{G_i-G_j}) v';  S = e^{G_last} S + (k e^{G_last-G})^T v'.
+    """
+    dtype = q.dtype
+    q = l2norm(q.float()) * q.shape[-1] ** -0.5
+    k = l2norm(k.float())
+    v, g, beta = v.float(), g.float(), beta.float()
+    b, s, h, dk = k.shape
+    dv = v.shape[-1]
+    pad = (-s) % chunk
+    if pad:
+        z = lambda t: F.pad(t, (0, 0, 0, 0, 0, pad)) if t.dim() == 4 else F.pad(t, (0, 0, 0, pad))  # noqa: E731
+        q, k, v, g, beta = z(q), z(k), z(v), z(g), z(beta)
+    n = (s + pad) // chunk
+    # [b, h, n, C, d]
+    r = lambda t: t.view(b, n, chunk, h, -1).permute(0, 3, 1, 2, 4)  # noqa: E731
+    q, k, v = r(q), r(k), r(v)
+    g = g.view(b, n, chunk, h).permute(0, 3, 1, 2).cumsum(-1)
+    beta = beta.view(b, n, chunk, h).permute(0, 3, 1, 2)
+    eye = torch.eye(chunk, device=q.device)
+    strict = torch.ones(chunk, chunk, device=q.device, dtype=torch.bool).tril(-1)
+    incl = torch.ones(chunk, chunk, device=q.device, dtype=torch.bool).tril()
+    decay = torch.where(incl, (g.unsqueeze(-1) - g.unsqueeze(-2)).clamp(max=0).exp(), torch.zeros((), device=q.device))
+    kb = k * beta.unsqueeze(-1)
+    m = torch.where(strict, (kb @ k.transpose(-1, -2)) * decay, torch.zeros((), device=q.device))
+    tinv = torch.linalg.solve_triangular(eye + m, eye.expand_as(m), upper=False, unitriangular=True)
+    u = tinv @ (v * beta.unsqueeze(-1))
+    w = tinv @ (kb * g.exp().unsqueeze(-1))
+    state = torch.zeros(b, h, dk, dv, device=q.device)
+    out = torch.empty(b, h, n, chunk, dv, device=q.device)
+    for i in range(n):
+        gi = g[:, :, i]
+        vn = u[:, :, i] - w[:, :, i] @ state
+        att = torch.where(incl, (q[:, :, i] @ k[:, :, i].transpose(-1, -2)) * decay[:, :, i],
+                          torch.zeros((), device=q.device))
+        out[:, :, i] = (q[:, :, i] * gi.exp().unsqueeze(-1)) @ state + att @ vn
+        last = gi[..., -1:]
+        state = state * last.exp().unsqueeze(-1) + (k[:, :, i] * (last - gi).exp().unsqueeze(-1)).transpose(-1, -2) @ vn
+    out = out.permute(0, 2, 3, 1, 4).reshape(b, n * chunk, h, dv)[:, :s]
+    return out.to(dtype)
+
+
+def causal_attention(q, k, v):
+    """Verifier attention: q [b, s, Hq, D], k/v [b, s, Hk, D]; bf16 scores + fp32 softmax."""
+    g = q.shape[2] // k.shape[2]
+    qt, kt, vt = q.transpose(1, 2), k.repeat_interleave(g, 2).transpose(1, 2), v.repeat_interleave(g, 2).transpose(1, 2)
+    s = (qt @ kt.transpose(-1, -2)) * q.shape[-1] ** -0.5
+    n = q.shape[1]
+    mask = torch.ones(n, n, dtype=torch.bool, device=q.device).triu(1)
+    s = s.masked_fill(mask, torch.finfo(s.dtype).min)
+    p = s.softmax(-1, dtype=torch.float32).to(q.dtype)
+    return (p @ vt).transpose(1, 2)
+
+
+def partial_rope(x, cos, sin, rotary_dim):
+    """RoPE on the first ``rotary_dim`` channels of each head. x [b, s, H, D]; cos/sin [b, s, rd]."""
+    c, s_ = cos.unsqueeze(2), sin.unsqueeze(2)
+    return torch.cat((rope(x[..., :rotary_dim], c, s_), x[..., rotary_dim:]), -1)

@@ -1,0 +1,135 @@
+"""Verifier (frozen Qwen3.5 hybrid) ops: forward only.
+
+CUDA tensors run the sm_100a kernels of ``nanospec_b200._C``; CPU tensors run the
+plain PyTorch statements in ``ops.reference`` (reference math:
+nanospec/ops.py:85-239 and the verifier loop of nanospec/train.py:53-157).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as ref
+from ._ext import cuda_ops
+
+
+def _c():
+    return cuda_ops()
+
+
+def embedding(ids, w):
+    if w.is_cuda:
+        out = torch.empty(*ids.shape, w.shape[1], device=w.device, dtype=w.dtype)
+        _c().embedding_fwd(ids.reshape(-1).contiguous(), w, out.view(-1, w.shape[1]))
+        return out
+    return F.embedding(ids, w)
+
+
+def add(x, y):
+    """x + y in the compute dtype (one rounding)."""
+    if x.is_cuda:
+        out = torch.empty_like(x)
+        _c().add_bf16(x.contiguous(), y.contiguous(), out)
+        return out
+    return x + y
+
+
+def silu_mul(gate, up):
+    """bf16(bf16(silu(gate)) * up)."""
+    if gate.is_cuda:
+        m = gate.shape[-1]
+        out = torch.empty_like(gate)
+        _c().silu_mul(gate.contiguous().view(-1, m), up.contiguous().view(-1, m), out.view(-1, m))
+        return out
+    return F.silu(gate) * up
+
+
+def qwen_norm(x, w, eps):
+    """(1 + w)-RMSNorm over the last dim, fp32 inside, one cast."""
+    if x.is_cuda:
+        n = x.shape[-1]
+        out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+        _c().qwen_norm(x.reshape(-1, n) if x.is_contiguous() else x.contiguous().view(-1, n), w, float(eps),
+                       out.view(-1, n))
+        return out
+    return ref.qwen_norm(x, w, eps)
+
+
+def qwen_gated_norm(x, gate, w, eps):
+    if x.is_cuda:
+        n = x.shape[-1]
+        out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+        _c().gated_norm(x.contiguous().view(-1, n), gate.contiguous().view(-1, n), w, float(eps), out.view(-1, n))
+        return out
+    return ref.qwen_gated_norm(x, gate, w, eps)
+
+
+def fp8_linear(x, w, scale_inv):
+    """Block-scaled FP8 projection (1 x 128 dynamic activations, 128 x 128 weight blocks)."""
+    if x.is_cuda:
+        n_out = w.shape[0]
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        out = torch.empty(x2.shape[0], n_out, device=x.device, dtype=x.dtype)
+        if w.dtype == torch.float8_e4m3fn:
+            _c().fp8_linear(x2.contiguous(), w, scale_inv, out)
+        else:
+            _c().linear(x2.contiguous(), w, out, None)
+        return out.view(*lead, n_out)
+    return ref.fp8_linear(x, w, scale_inv)
+
+
+def causal_conv_silu(x, w):
+    """Depthwise causal conv (kernel K) + SiLU over tokens; x [b, s, C] token-major."""
+    if x.is_cuda:
+        out = torch.empty_like(x)
+        _c().conv_silu(x.contiguous(), w.reshape(w.shape[0], -1).contiguous(), out)
+        return out
+    return ref.causal_conv_silu(x, w)
+
+
+def gdn_gates(a, b, a_log, dt_bias):
+    if a.is_cuda:
+        g = torch.empty(a.shape, device=a.device, dtype=torch.float32)
+        beta = torch.empty(b.shape, device=b.device, dtype=b.dtype)
+        _c().gdn_gates(a.contiguous(), b.contiguous(), a_log.float().contiguous(), dt_bias.float().contiguous(), g, beta)
+        return g, beta
+    return ref.gdn_gates(a, b, a_log, dt_bias)
+
+
+def gated_delta_rule(q, k, v, g, beta, groups=1, chunk=64):
+    """Gated delta rule with GQA: value head h uses key head h // groups.
+
+    q, k [b, s, nk, dk]; v [b, s, nv, dv]; g [b, s, nv] fp32; beta [b, s, nv].
+    """
+    if q.is_cuda:
+        out = torch.empty(v.shape, device=v.device, dtype=v.dtype)
+        _c().gdn_chunk_fwd(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(), beta.contiguous(),
+                           int(groups), out)
+        return out
+    if groups > 1:
+        q = q.repeat_interleave(groups, 2)
+        k = k.repeat_interleave(groups, 2)
+    return ref.gated_delta_rule_chunked(q, k, v, g, beta, chunk)
+
+
+def rotary_factors(positions, dim, theta, dtype):
+    return ref.rotary_factors(positions, dim, theta, dtype)
+
+
+def causal_attention_gated(q, k, v, gate, cos, sin, rotary_dim):
+    """Partial RoPE on q/k, causal GQA attention, then ``out * sigmoid(gate)``.
+
+    q [b, s, Hq, D] and k, v [b, s, Hk, D] (q, k already (1+w)-normalised); gate
+    [b, s, Hq, D]; cos/sin [b, s, rotary_dim]. Returns [b, s, Hq, D].
+    """
+    if q.is_cuda:
+        out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+        _c().causal_attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), gate.contiguous(),
+                             cos[0].contiguous(), sin[0].contiguous(), int(rotary_dim), out)
+        return out
+    q = ref.partial_rope(q, cos, sin, rotary_dim)
+    k = ref.partial_rope(k, cos, sin, rotary_dim)
+    o = ref.causal_attention(q, k, v)
+    return o * gate.sigmoid()

@@ -199,7 +199,8 @@ class ShardingPlan:
         ``resident`` (gathered weights kept from the forward for the backward).
         """
         seq = tuple(self.step_sequence() if sequence is None else sequence)
-        if self.context.world_size == 1 or (not overlap and not resident):
+        on_cpu = self.context.param.device.type != "cuda"  # side streams exist on CUDA only
+        if self.context.world_size == 1 or on_cpu or (not overlap and not resident):
             return SerialSchedule(seq)
         key = "resident" if resident else "overlap"
         sched = self._cache.get(key)

@@ -35,10 +35,11 @@ def _seed():
 
 
 @cuda
-@pytest.mark.parametrize("M,N,K", [(128, 64, 64), (256, 128, 512), (300, 200, 1000), (1024, 256, 4096),
-                                   (128, 192, 128), (5120, 56, 5120)])
+@pytest.mark.parametrize("M,N,K", [(128, 64, 64), (256, 128, 512), (304, 200, 1000), (1024, 256, 4096),
+                                   (128, 192, 128), (5120, 56, 5120), (96, 40, 64)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
 def test_gemm_majors(M, N, K, a_mn, b_mn):
+    # TMA needs 16-byte row strides: the contiguous dimension of each operand is a multiple of 8.
     dev = "cuda"
     a = torch.randn(M, K, device=dev).bfloat16()
     b = torch.randn(N, K, device=dev).bfloat16()

@@ -1,0 +1,108 @@
+"""Verifier kernels (FP8 GEMM, GDN, conv, norms, attention) vs the CPU statements."""
+
+import pytest
+import torch
+
+from nanospec_b200.ops import reference as ref
+from nanospec_b200.ops import verifier_ops as vops
+
+pytestmark = pytest.mark.gpu
+cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+
+
+def close(a, b, rtol=2e-2, cos_min=0.999):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    scale = b.abs().max().item() + 1e-6
+    cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+    assert err <= rtol * scale + 1e-3, f"max err {err} vs scale {scale}"
+    assert cos > cos_min, f"cos {cos}"
+
+
+@pytest.fixture(autouse=True)
+def _check():
+    torch.manual_seed(0)
+    yield
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        from nanospec_b200.ops._ext import cuda_ops
+        assert cuda_ops().device_error() == 0
+
+
+@cuda
+@pytest.mark.parametrize("T,K,N", [(200, 512, 384), (16, 256, 128), (1000, 1024, 640)])
+def test_fp8_linear(T, K, N):
+    from nanospec_b200.models.verifier import quantize_weight_blocks
+    x = torch.randn(T, K).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K) * 0.05)
+    expect = ref.fp8_linear(x, w, s)
+    got = vops.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    close(got, expect, rtol=1e-2, cos_min=0.9999)
+
+
+@cuda
+def test_small_verifier_ops():
+    x = torch.randn(3, 50, 96).bfloat16()
+    w = (torch.randn(96) * 0.1).bfloat16()
+    close(vops.qwen_norm(x.cuda(), w.cuda(), 1e-6), ref.qwen_norm(x, w, 1e-6), rtol=1e-2)
+    gt = torch.randn(150, 96).bfloat16()
+    close(vops.qwen_gated_norm(x.view(-1, 96).cuda(), gt.cuda(), w.cuda(), 1e-6),
+          ref.qwen_gated_norm(x.view(-1, 96), gt, w, 1e-6), rtol=2e-2)
+    cw = (torch.randn(96, 1, 4) * 0.3).bfloat16()
+    close(vops.causal_conv_silu(x.cuda(), cw.cuda()), ref.causal_conv_silu(x, cw), rtol=2e-2)
+    a, b = torch.randn(3, 50, 6).bfloat16(), torch.randn(3, 50, 6).bfloat16()
+    alog, dtb = torch.randn(6), torch.rand(6)
+    g1, b1 = vops.gdn_gates(a.cuda(), b.cuda(), alog.cuda(), dtb.cuda())
+    g2, b2 = ref.gdn_gates(a, b, alog, dtb)
+    close(g1, g2, rtol=1e-3)
+    close(b1, b2, rtol=1e-2)
+
+
+@cuda
+@pytest.mark.parametrize("D,s,groups", [(16, 100, 2), (128, 130, 3)])
+def test_gated_delta_rule(D, s, groups):
+    b, nk = 2, 2
+    nv = nk * groups
+    q = torch.randn(b, s, nk, D).bfloat16()
+    k = torch.randn(b, s, nk, D).bfloat16()
+    v = torch.randn(b, s, nv, D).bfloat16()
+    g = -torch.rand(b, s, nv) * 0.5
+    beta = torch.rand(b, s, nv).bfloat16()
+    got = vops.gated_delta_rule(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), groups)
+    expect = ref.gated_delta_rule_recurrent(q.repeat_interleave(groups, 2).double(),
+                                            k.repeat_interleave(groups, 2).double(), v.double(), g.double(),
+                                            beta.double())
+    close(got, expect, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+@pytest.mark.parametrize("D,rd,hq,hk,s", [(32, 16, 4, 2, 70), (256, 64, 6, 2, 150)])
+def test_causal_attention_gated(D, rd, hq, hk, s):
+    b = 2
+    q = torch.randn(b, s, hq, D).bfloat16()
+    k = torch.randn(b, s, hk, D).bfloat16()
+    v = torch.randn(b, s, hk, D).bfloat16()
+    gate = torch.randn(b, s, hq, D).bfloat16()
+    pos = torch.arange(s).expand(b, s)
+    cos, sin = ref.rotary_factors(pos, rd, 1e6, torch.bfloat16)
+    expect = vops.causal_attention_gated(q, k, v, gate, cos, sin, rd)
+    got = vops.causal_attention_gated(q.cuda(), k.cuda(), v.cuda(), gate.cuda(), cos.cuda(), sin.cuda(), rd)
+    close(got, expect, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+def test_stage_forward_matches_cpu(tmp_path):
+    from nanospec_b200.models.verifier import (Checkpoint, QwenStage, stage_forward, tiny_hybrid_text_config,
+                                               write_synthetic_checkpoint)
+    tc = tiny_hybrid_text_config(hidden=128, vocab=512, heads=4, head_dim=32, ffn=256)
+    path = write_synthetic_checkpoint(tmp_path / "ckpt", tc, seed=1, fp8=True)
+    ck = Checkpoint(path)
+    ids = torch.randint(0, 512, (2, 96))
+    outs = {}
+    for dev in ("cpu", "cuda"):
+        st = QwenStage(ck, 0, 4, device=dev, first=True, last=True)
+        x, cap = stage_forward(st, ids.to(dev), capture=(1, 3))
+        outs[dev] = (x, cap)
+    close(outs["cuda"][0], outs["cpu"][0], rtol=5e-2, cos_min=0.995)
+    for i in (1, 3):
+        close(outs["cuda"][1][i], outs["cpu"][1][i], rtol=5e-2, cos_min=0.995)
