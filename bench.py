@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true")
+    p.add_argument("--comm", choices=("peer", "nccl"), default="peer",
+                   help="N>1: peer-memory kernels over NVLink (default) or NCCL collectives")
     return p.parse_args()
 
 
@@ -197,6 +199,8 @@ def main():
         o = N.Objective(num_anchors=args.anchors)
     else:
         o = RObjective(num_anchors=args.anchors)
+    if args.impl == "ours" and world > 1 and args.comm == "peer":
+        model.sharding.enable_peer()
     ids, states, last, mask = synthetic_batch(c, args.seq_len, rank, args.seed, dev, dtype)
     batch = TB(states, last)
 
@@ -288,6 +292,7 @@ def main():
                          f"vocab {c.vocab_size}) + frozen target embed/LM head",
                 "global_batch": n, "seq_len": args.seq_len, "anchors": args.anchors,
                 "block_size": 7, "parallelism": f"fsdp{n}" if n > 1 else "single",
+                "comm": (args.comm if args.impl == "ours" else "nccl") if n > 1 else None,
                 "optimizer": "AdamW fp32 masters, lr 1e-5, wd 0.01",
                 "l2": "per-step working set (weights, fp32 masters and moments) far exceeds the 126 MB L2",
             },
@@ -300,6 +305,8 @@ def main():
             out["impl"] = "reference"
         print(json.dumps(out), flush=True)
     if world > 1:
+        if args.impl == "ours":
+            model.sharding.close_peer()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -268,23 +268,26 @@ __global__ void __launch_bounds__(256) attn_bwd_dq_kernel(AttnArgs a) {
 
 // ---------------------------------------------------------------------------- backward dk, dv
 // Tiles: ctx tiles [0, ceil(S/KT)) then one tile per draft block (bs <= 32).
-// Thread layout: warp w handles query rows w, w+nw, ...; lane = key within the tile;
-// dK/dV accumulate in shared memory (transposed [D][KT]) via one owner lane per key.
+// For each query block j that sees the tile: warps compute P and dS for the block's
+// rows (lane = key) into shared memory; then thread (key = t % 32, dim chunk t / 32)
+// accumulates dK[key] += dS * q and dV[key] += P * dO over the rows in registers.
 template <int D>
 __global__ void __launch_bounds__(128) attn_bwd_dkv_kernel(AttnArgs a) {
-  constexpr int E = (D + 31) / 32;
-  constexpr int DL = D < 32 ? D : 32;
+  constexpr int NT = 128;
+  constexpr int DC = D / (NT / 32);  // dims per thread in the accumulation phase
+  constexpr int RMAX = 64;
   extern __shared__ float sm[];
+  float* Kt = sm;                 // [D][KT]
+  float* Vt = Kt + D * KT;        // [D][KT]
+  float* Qs = Vt + D * KT;        // [RMAX][D]  (q, unscaled)
+  float* Os = Qs + RMAX * D;      // [RMAX][D]  (dO)
+  float* Ps = Os + RMAX * D;      // [RMAX][KT]
+  float* DSs = Ps + RMAX * KT;    // [RMAX][KT]
   const int tile = blockIdx.x, hk = blockIdx.y, bi = blockIdx.z;
   const int G = a.Hq / a.Hk;
   const int Td = a.nb * a.bs;
   const int nctx = (a.S + KT - 1) / KT;
-  float* Kt = sm;              // [D][KT]
-  float* Vt = Kt + D * KT;     // [D][KT]
-  float* dKt = Vt + D * KT;    // [NW][D][KT] per-warp partials
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  float* mydK = dKt + warp * 2 * D * KT;
-  float* mydV = mydK + D * KT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = NT / 32;
   int k0, cnt, jlo, jhi;
   if (tile < nctx) {
     k0 = tile * KT;
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(128) attn_bwd_dkv_kernel(AttnArgs a) {
     jlo = jb;
     jhi = jb + 1;
   }
-  for (int idx = threadIdx.x; idx < KT * D; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < KT * D; idx += NT) {
     const int kk = idx / D, d = idx % D;
     float kvv = 0.f, vvv = 0.f;
     if (kk < cnt) {
@@ -309,71 +312,64 @@ __global__ void __launch_bounds__(128) attn_bwd_dkv_kernel(AttnArgs a) {
     Kt[d * KT + kk] = kvv;
     Vt[d * KT + kk] = vvv;
   }
-  for (int idx = threadIdx.x; idx < nw * 2 * D * KT; idx += blockDim.x) dKt[idx] = 0.f;
-  __syncthreads();
+  const int key = threadIdx.x & 31;
+  const int d0 = (threadIdx.x >> 5) * DC;
+  float dK[DC], dV[DC];
+#pragma unroll
+  for (int i = 0; i < DC; ++i) dK[i] = dV[i] = 0.f;
   const int R = G * a.bs;
   for (int j = jlo; j < jhi; ++j) {
     if (!a.keep[bi * a.nb + j]) continue;
     const int anchor = (int)a.anchors[bi * a.nb + j];
-    // visible count within this tile for block j
-    int vis;
-    if (tile < nctx) vis = max(0, min(cnt, anchor - k0));
-    else vis = cnt;
+    const int vis = tile < nctx ? max(0, min(cnt, anchor - k0)) : cnt;
     if (vis <= 0) continue;
+    __syncthreads();  // previous block's Ps/DSs/Qs/Os fully consumed
+    for (int idx = threadIdx.x; idx < R * D; idx += NT) {
+      const int r = idx / D, d = idx % D;
+      const int g = r / a.bs, u = r % a.bs;
+      const int t = bi * Td + j * a.bs + u;
+      const int64_t off = ((int64_t)t * a.Hq + hk * G + g) * D + d;
+      Qs[r * D + d] = __bfloat162float(a.q[off]);
+      Os[r * D + d] = __bfloat162float(a.dout[off]);
+    }
+    __syncthreads();
     for (int r = warp; r < R; r += nw) {
       const int g = r / a.bs, u = r % a.bs;
       const int h = hk * G + g;
       const int t = bi * Td + j * a.bs + u;
       const int64_t off = ((int64_t)t * a.Hq + h) * D;
-      float qv[E], dov[E];
       float dl = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const bool in = lane < DL;
-        qv[e] = in ? __bfloat162float(a.q[off + lane + 32 * e]) : 0.f;
-        dov[e] = in ? __bfloat162float(a.dout[off + lane + 32 * e]) : 0.f;
-        dl += in ? dov[e] * __bfloat162float(a.o[off + lane + 32 * e]) : 0.f;
-      }
+      for (int d = lane; d < D; d += 32) dl += Os[r * D + d] * __bfloat162float(a.o[off + d]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(0xffffffff, dl, o);
       const float lse = a.lse[((int64_t)bi * a.Hq + h) * Td + j * a.bs + u];
       float s = 0.f, dp = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
 #pragma unroll 8
-        for (int dd = 0; dd < DL; ++dd) {
-          const float qd = __shfl_sync(0xffffffff, qv[e], dd);
-          const float od = __shfl_sync(0xffffffff, dov[e], dd);
-          s += qd * Kt[(dd + 32 * e) * KT + lane];
-          dp += od * Vt[(dd + 32 * e) * KT + lane];
-        }
+      for (int d = 0; d < D; ++d) {
+        s += Qs[r * D + d] * Kt[d * KT + lane];
+        dp += Os[r * D + d] * Vt[d * KT + lane];
       }
       const float p = (lane < vis && lse > -INFINITY) ? expf(s * a.scale - lse) : 0.f;
-      const float ds = p * (dp - dl) * a.scale;
-      // lane = key owner: dV[key] += p * dO, dK[key] += ds * q  (q unscaled)
+      Ps[r * KT + lane] = p;
+      DSs[r * KT + lane] = p * (dp - dl) * a.scale;
+    }
+    __syncthreads();
+    for (int r = 0; r < R; ++r) {
+      const float p = Ps[r * KT + key], ds = DSs[r * KT + key];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-#pragma unroll 8
-        for (int dd = 0; dd < DL; ++dd) {
-          const float qd = __shfl_sync(0xffffffff, qv[e], dd);
-          const float od = __shfl_sync(0xffffffff, dov[e], dd);
-          mydK[(dd + 32 * e) * KT + lane] += ds * qd;
-          mydV[(dd + 32 * e) * KT + lane] += p * od;
-        }
+      for (int i = 0; i < DC; ++i) {
+        dV[i] += p * Os[r * D + d0 + i];
+        dK[i] += ds * Qs[r * D + d0 + i];
       }
     }
   }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < cnt * D; idx += blockDim.x) {
-    const int kk = idx / D, d = idx % D;
-    float sk = 0.f, sv = 0.f;
-    for (int w = 0; w < nw; ++w) {
-      sk += dKt[w * 2 * D * KT + d * KT + kk];
-      sv += dKt[w * 2 * D * KT + D * KT + d * KT + kk];
+  if (key < cnt) {
+    const int64_t row = key_row(a, bi, k0 + key);
+#pragma unroll
+    for (int i = 0; i < DC; ++i) {
+      a.dk[row * a.lddk + hk * D + d0 + i] = __float2bfloat16(dK[i]);
+      a.dv[row * a.lddv + hk * D + d0 + i] = __float2bfloat16(dV[i]);
     }
-    const int64_t row = key_row(a, bi, k0 + kk);
-    a.dk[row * a.lddk + hk * D + d] = __float2bfloat16(sk);
-    a.dv[row * a.lddv + hk * D + d] = __float2bfloat16(sv);
   }
 }
 
@@ -427,7 +423,7 @@ static void bwd_d(AttnArgs a) {
     NS_CUDA(cudaGetLastError());
   }
   {
-    const int smem = (2 + 4 * 2) * D * KT * 4;
+    const int smem = (2 * D * KT + 2 * 64 * D + 2 * 64 * KT) * 4;
     NS_CUDA(cudaFuncSetAttribute(attn_bwd_dkv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int tiles = (a.S + KT - 1) / KT + a.nb;
     dim3 grid(tiles, a.Hk, a.b);

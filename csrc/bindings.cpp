@@ -44,6 +44,15 @@ void gdn_gates(at::Tensor a, at::Tensor b, at::Tensor alog, at::Tensor dtb, at::
 void gdn_chunk_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, int64_t groups, at::Tensor out);
 void causal_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor gate, at::Tensor cs, at::Tensor sn, int64_t rd,
                      at::Tensor out);
+std::vector<int64_t> window_create(int64_t bytes, int64_t rank, int64_t world);
+at::Tensor window_ipc_handle(int64_t id);
+void window_open(int64_t id, at::Tensor handles);
+void window_close(int64_t id);
+at::Tensor window_view(int64_t id, int64_t offset, int64_t numel, at::ScalarType dtype);
+void peer_allgather(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out);
+void peer_reduce_avg(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad);
+void peer_signal(int64_t id, int64_t flags_off, int64_t channel, int64_t seq);
+void peer_wait(int64_t id, int64_t flags_off, int64_t channel, int64_t seq, int64_t poll_limit);
 int64_t device_error();
 void clear_device_error();
 }  // namespace ns
@@ -76,6 +85,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_gates", &ns::gdn_gates);
   m.def("gdn_chunk_fwd", &ns::gdn_chunk_fwd);
   m.def("causal_attn_fwd", &ns::causal_attn_fwd);
+  m.def("window_create", &ns::window_create);
+  m.def("window_ipc_handle", &ns::window_ipc_handle);
+  m.def("window_open", &ns::window_open);
+  m.def("window_close", &ns::window_close);
+  m.def("window_view", &ns::window_view);
+  m.def("peer_allgather", &ns::peer_allgather);
+  m.def("peer_reduce_avg", &ns::peer_reduce_avg);
+  m.def("peer_signal", &ns::peer_signal);
+  m.def("peer_wait", &ns::peer_wait);
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
   m.def("clear_device_error", &ns::clear_device_error);
 }

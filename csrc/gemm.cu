@@ -9,13 +9,19 @@
 // the output is written transposed.
 //
 // One CTA = one 128 x BN output tile over a K range (split-K across blockIdx.z):
-//   warp 0   : one thread issues TMA loads into a STAGES-deep smem ring;
+//   warp 0   : one thread issues TMA loads into a `stages`-deep smem ring;
 //   warp 1   : allocates TMEM; one thread issues tcgen05.mma (K = 16 per issue)
 //              and commits each stage back to the producer;
 //   warps 2-5: epilogue, tcgen05.ld of the accumulator (each warp owns the TMEM
-//              lane quarter warp % 4), then bf16 stores with optional residual /
-//              accumulate, or fp32 partials for the deterministic split-K reduce.
+//              lane quarter warp % 4), then bf16/fp32 stores with optional
+//              residual / accumulate.
+// Split-K: every split writes an fp32 partial; the last CTA of a tile to finish
+// (per-tile arrival counter) sums the partials in split order 0..S-1 and runs the
+// epilogue, so results are deterministic and no second kernel is launched.
+// Grids are sized so all CTAs are co-resident (two per SM): one full wave.
 // Every mbarrier wait is bounded; a timeout sets the device error flag.
+#include <map>
+
 #include "common.h"
 #include "gemm.h"
 #include "sm100.cuh"
@@ -27,16 +33,17 @@ constexpr int BK = 64;
 
 struct GemmArgs {
   int M, N, K;
-  int kpb;      // k-blocks per split
+  int kpb;  // k-blocks per split
   int splits;
-  float* out_f32;               // fp32 output (accumulate adds), used instead of `out` when set
+  float* out_f32;  // fp32 output (accumulate adds), used instead of `out` when set
   __nv_bfloat16* out;
-  int64_t out_sm, out_sn;       // element strides of out(m, n)
-  const __nv_bfloat16* res;     // optional residual, same addressing as out
+  int64_t out_sm, out_sn;    // element strides of out(m, n)
+  const __nv_bfloat16* res;  // optional residual, same addressing as out
   int64_t res_sm, res_sn;
-  int accumulate;               // out = out + D
-  float* ws;                    // split-K partials
-  int ws_t;                     // partial layout: 0 -> [s][m][n], 1 -> [s][n][m]
+  int accumulate;  // out = out + D
+  float* ws;       // split-K partials [splits][M][N] (ws_t: [splits][N][M])
+  int ws_t;
+  unsigned* counters;  // per-tile arrival counters (zero between launches)
   int* err;
 };
 
@@ -45,10 +52,10 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  // Ring depth chosen so two CTAs fit on one SM (228 KB of shared memory).
+  static constexpr int STAGES = (110 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_MAX = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
 __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, float acc) {
@@ -62,6 +69,31 @@ __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, flo
   __nv_bfloat16* p = a.out + m * a.out_sm + n * a.out_sn;
   if (a.accumulate) y = sm100::bf16_round(__bfloat162float(*p) + y);
   *p = __float2bfloat16(y);
+}
+
+// Epilogue of 32 consecutive columns [nb, nb+32) of row m.
+__device__ __forceinline__ void store_row32(const GemmArgs& a, int m, int nb, const float (&v)[32]) {
+  if (!a.out_f32 && a.out_sn == 1 && !a.res && !a.accumulate && nb + 32 <= a.N && (a.out_sm % 8) == 0) {
+    uint4* p = reinterpret_cast<uint4*>(a.out + m * a.out_sm + nb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 h[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(v[8 * j + 2 * t], v[8 * j + 2 * t + 1]);
+      p[j] = *reinterpret_cast<uint4*>(h);
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = nb + j;
+    if (n < a.N) store_final(a, m, n, v[j]);
+  }
+}
+
+__device__ __forceinline__ int64_t ws_index(const GemmArgs& a, int s, int m, int n) {
+  const int64_t base = (int64_t)s * a.M * a.N;
+  return base + (a.ws_t ? (int64_t)n * a.M + m : (int64_t)m * a.N + n);
 }
 
 template <int BN, bool AMN, bool BMN>
@@ -78,6 +110,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint32_t* last_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, split = blockIdx.z;
@@ -157,12 +190,12 @@ __global__ void __launch_bounds__(192, 1)
       }
       sm100::mma_commit(acc_full);
     }
-  } else {
-    const int q = warp & 3;
-    const bool ok = sm100::mbar_wait(acc_full, 0, args.err);
-    if (ok) {
+  }
+  const int q = warp & 3;
+  const int m = m0 + q * 32 + lane;
+  if (warp >= 2) {
+    if (sm100::mbar_wait(acc_full, 0, args.err)) {
       sm100::tc_fence_after();
-      const int m = m0 + q * 32 + lane;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -170,34 +203,17 @@ __global__ void __launch_bounds__(192, 1)
         if (m >= args.M) continue;
         const int nb = n0 + c;
         if (args.splits > 1) {
-          float* ws = args.ws + (int64_t)split * args.M * args.N;
           if (!args.ws_t && nb + 32 <= args.N && (args.N % 4) == 0) {
-            float4* p = reinterpret_cast<float4*>(ws + (int64_t)m * args.N + nb);
+            float4* p = reinterpret_cast<float4*>(args.ws + ws_index(args, split, m, nb));
 #pragma unroll
             for (int j = 0; j < 8; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = nb + j;
-              if (n < args.N) ws[args.ws_t ? (int64_t)n * args.M + m : (int64_t)m * args.N + n] = v[j];
-            }
-          }
-        } else if (!args.out_f32 && args.out_sn == 1 && !args.res && !args.accumulate && nb + 32 <= args.N &&
-                   (args.out_sm % 8) == 0) {
-          uint4* p = reinterpret_cast<uint4*>(args.out + m * args.out_sm + nb);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            __nv_bfloat162 h[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(v[8 * j + 2 * t], v[8 * j + 2 * t + 1]);
-            p[j] = *reinterpret_cast<uint4*>(h);
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < args.N) args.ws[ws_index(args, split, m, nb + j)] = v[j];
           }
         } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = nb + j;
-            if (n < args.N) store_final(args, m, n, v[j]);
-          }
+          store_row32(args, m, nb, v);
         }
       }
     }
@@ -208,52 +224,85 @@ __global__ void __launch_bounds__(192, 1)
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, C::TMEM_COLS);
   }
-}
-
-// Deterministic split-K reduction (fixed split order) + the final epilogue.
-__global__ void splitk_reduce_kernel(GemmArgs a) {
-  const int64_t total = (int64_t)a.M * a.N;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    float acc = 0.f;
-    for (int s = 0; s < a.splits; ++s) acc += a.ws[s * total + i];
-    int m, n;
-    if (a.ws_t) {
-      n = (int)(i / a.M);
-      m = (int)(i % a.M);
-    } else {
-      m = (int)(i / a.N);
-      n = (int)(i % a.N);
+  if (args.splits > 1) {
+    // Arrival: the last split CTA of this tile reduces all partials in order.
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      const unsigned prev = atomicAdd(&args.counters[tile], 1u);
+      const bool last = prev == (unsigned)(args.splits - 1);
+      if (last) args.counters[tile] = 0;  // reset for the next launch on this stream
+      *last_flag = last ? 1u : 0u;
     }
-    store_final(a, m, n, acc);
+    __syncthreads();
+    if (*last_flag) {
+      __threadfence();
+      // Groups of 4 consecutive elements along the partials' contiguous dimension;
+      // all split loads of a group are issued before the ordered sum.
+      const int inner = args.ws_t ? BM : BN;   // contiguous extent inside the tile
+      const int outer = args.ws_t ? BN : BM;
+      const int ginner = inner / 4;
+      const int64_t ld = args.ws_t ? args.M : args.N;
+      const bool vec = (ld % 4) == 0;
+      for (int g = threadIdx.x; g < ginner * outer; g += blockDim.x) {
+        const int o = g / ginner, i4 = (g % ginner) * 4;
+        const int gm0 = args.ws_t ? m0 + i4 : m0 + o;
+        const int gn0 = args.ws_t ? n0 + o : n0 + i4;
+        if (gm0 >= args.M || gn0 >= args.N) continue;
+        const int lim = args.ws_t ? args.M - gm0 : args.N - gn0;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (vec && lim >= 4) {
+          float4 part[8];
+          for (int s0 = 0; s0 < args.splits; s0 += 8) {
+            const int ns = min(8, args.splits - s0);
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+              if (s < ns) part[s] = __ldcg(reinterpret_cast<const float4*>(args.ws + ws_index(args, s0 + s, gm0, gn0)));
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+              if (s < ns) {
+                acc[0] += part[s].x;
+                acc[1] += part[s].y;
+                acc[2] += part[s].z;
+                acc[3] += part[s].w;
+              }
+          }
+        } else {
+          for (int s = 0; s < args.splits; ++s)
+            for (int e = 0; e < 4 && e < lim; ++e)
+              acc[e] += __ldcg(args.ws + ws_index(args, s, args.ws_t ? gm0 + e : gm0, args.ws_t ? gn0 : gn0 + e));
+        }
+        for (int e = 0; e < 4 && e < lim; ++e)
+          store_final(args, args.ws_t ? gm0 + e : gm0, args.ws_t ? gn0 : gn0 + e, acc[e]);
+      }
+    }
   }
 }
 
 template <int BN, bool AMN, bool BMN>
-static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid) {
+static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, int stages) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, AMN, BMN>;
   static bool attr = false;
   if (!attr) {
-    NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_MAX));
     attr = true;
   }
-  // A CTA never needs more ring stages than it has k-blocks; a short K (weight
-  // gradients over a few dozen tokens) then uses little shared memory and several
-  // CTAs share an SM, overlapping one CTA's epilogue with another's loads.
-  const int stages = std::max(1, std::min(C::STAGES, a.kpb));
-  const int smem = stages * C::STAGE_BYTES + 1024 + 256;
+  // TMEM holds 512 columns per SM: reserve enough shared memory that no more CTAs
+  // co-reside than their accumulators fit (an allocation never has to wait).
+  const int min_smem = (228 * 1024) / (512 / C::TMEM_COLS) - 1024 + 1;
+  const int smem = std::max(stages * C::STAGE_BYTES + 1024 + 256, std::min(min_smem, C::SMEM_MAX));
   kern<<<grid, 192, smem, stream()>>>(ta, tb, a, stages);
   NS_CUDA(cudaGetLastError());
 }
 
 template <bool AMN, bool BMN>
-static void launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid) {
+static void launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, int stages) {
   switch (bn) {
-    case 64: launch_bn<64, AMN, BMN>(ta, tb, a, grid); break;
-    case 128: launch_bn<128, AMN, BMN>(ta, tb, a, grid); break;
-    case 192: launch_bn<192, AMN, BMN>(ta, tb, a, grid); break;
-    default: launch_bn<256, AMN, BMN>(ta, tb, a, grid); break;
+    case 64: launch_bn<64, AMN, BMN>(ta, tb, a, grid, stages); break;
+    case 128: launch_bn<128, AMN, BMN>(ta, tb, a, grid, stages); break;
+    case 192: launch_bn<192, AMN, BMN>(ta, tb, a, grid, stages); break;
+    default: launch_bn<256, AMN, BMN>(ta, tb, a, grid, stages); break;
   }
 }
 
@@ -264,9 +313,35 @@ static int pick_bn(int N) {
   return 256;
 }
 
+static int max_stages(int bn) {
+  switch (bn) {
+    case 64: return GemmCfg<64>::STAGES;
+    case 128: return GemmCfg<128>::STAGES;
+    case 192: return GemmCfg<192>::STAGES;
+    default: return GemmCfg<256>::STAGES;
+  }
+}
+
+// Per-(device, stream) arrival counters for split-K; each launch leaves them zero.
+static unsigned* split_counters(int tiles) {
+  static std::map<std::pair<int, cudaStream_t>, std::pair<unsigned*, int>> pool;
+  int dev;
+  NS_CUDA(cudaGetDevice(&dev));
+  auto key = std::make_pair(dev, stream());
+  auto it = pool.find(key);
+  if (it == pool.end() || it->second.second < tiles) {
+    const int n = std::max(tiles, 4096);
+    unsigned* p = nullptr;
+    NS_CUDA(cudaMalloc(&p, n * sizeof(unsigned)));
+    NS_CUDA(cudaMemsetAsync(p, 0, n * sizeof(unsigned), stream()));
+    pool[key] = std::make_pair(p, n);  // an older, smaller array stays allocated (launches in flight)
+    return p;
+  }
+  return it->second.first;
+}
+
 // D[M,N] = A * B^T with the epilogue `e`.
-void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e,
-                 int force_splits) {
+void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e, int force_splits) {
   NS_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
   const int bn = pick_bn(N);
   CUtensorMap ta = A.mn_major ? make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BK, 64)
@@ -276,15 +351,19 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   const int mt = (M + BM - 1) / BM, nt = (N + bn - 1) / bn;
   const int kb = (K + BK - 1) / BK;
   const int tiles = mt * nt;
+  // Split K only until every SM has one CTA: each extra split adds an fp32 partial
+  // round trip, which for the weight-streaming (small-N) products costs more than
+  // the second CTA per SM gains.
+  const int slots = num_sms();
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
-  } else if (tiles < num_sms()) {
-    splits = (num_sms() + tiles - 1) / tiles;
-    splits = std::min(splits, std::max(1, kb / 4));
+  } else if (tiles < slots) {
+    splits = std::max(1, std::min(slots / tiles, kb / 4));
   }
   int kpb = (kb + splits - 1) / splits;
   splits = (kb + kpb - 1) / kpb;
+  const int stages = std::max(1, std::min(max_stages(bn), kpb));
 
   GemmArgs a{};
   a.M = M;
@@ -306,18 +385,13 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   if (splits > 1) {
     ws = at::empty({(int64_t)splits * M * N}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA));
     a.ws = ws.data_ptr<float>();
+    a.counters = split_counters(tiles);
   }
   dim3 grid(mt, nt, splits);
-  if (!A.mn_major && !B.mn_major) launch<false, false>(bn, ta, tb, a, grid);
-  else if (A.mn_major && !B.mn_major) launch<true, false>(bn, ta, tb, a, grid);
-  else if (!A.mn_major && B.mn_major) launch<false, true>(bn, ta, tb, a, grid);
-  else launch<true, true>(bn, ta, tb, a, grid);
-  if (splits > 1) {
-    const int64_t total = (int64_t)M * N;
-    int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
-    splitk_reduce_kernel<<<blocks, 256, 0, stream()>>>(a);
-    NS_CUDA(cudaGetLastError());
-  }
+  if (!A.mn_major && !B.mn_major) launch<false, false>(bn, ta, tb, a, grid, stages);
+  else if (A.mn_major && !B.mn_major) launch<true, false>(bn, ta, tb, a, grid, stages);
+  else if (!A.mn_major && B.mn_major) launch<false, true>(bn, ta, tb, a, grid, stages);
+  else launch<true, true>(bn, ta, tb, a, grid, stages);
 }
 
 // ----------------------------------------------------------------------------- torch API

@@ -291,12 +291,24 @@ __global__ void embedding_bwd_kernel(const bf16* __restrict__ dy, const int64_t*
 
 // ------------------------------------------------------------------ optimizer
 // sum over the shard of bf16(g * factor)^2: per-block partial, fixed-order final sum.
+// 8 bf16 (16 bytes) per thread per iteration.
 __global__ void grad_norm_part_kernel(const bf16* __restrict__ g, int64_t n, const float* __restrict__ factor,
                                       float* __restrict__ part) {
   __shared__ float sh[32];
   const float fac = *factor;
   float s = 0.f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t n8 = n / 8;
+  const uint4* g8 = reinterpret_cast<const uint4*>(g);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 raw = g8[i];
+    const bf16* h = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = r(f(h[j]) * fac);
+      s += v * v;
+    }
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = r(f(g[i]) * fac);
     s += v * v;
   }
@@ -312,27 +324,67 @@ __global__ void sum_into_kernel(const float* __restrict__ part, int parts, float
   }
 }
 
-__global__ void adamw_kernel(bf16* __restrict__ param, float* __restrict__ master, float* __restrict__ m,
-                             float* __restrict__ v, bf16* __restrict__ grad, int64_t n,
-                             const float* __restrict__ factor, const float* __restrict__ norm2, float lr,
-                             float wd, float b1, float b2, float eps, float bc1, float bc2, float max_norm) {
+struct AdamHyper {
+  float lr, wd, b1, b2, eps, bc1, bc2, max_norm;
+};
+
+__device__ __forceinline__ void adam_one(float g, float& w, float& mm, float& vv, float decay, float step,
+                                         const AdamHyper& h) {
+  mm = mm + (1.f - h.b1) * (g - mm);
+  vv = h.b2 * vv + (1.f - h.b2) * g * g;
+  const float denom = sqrtf(vv) / h.bc2 + h.eps;
+  w = w * decay - step * (mm / denom);
+}
+
+// Fused AdamW over one flat shard: reads grad (bf16), master/m/v (fp32); writes
+// master/m/v, param (bf16) and zeroes grad. 4 elements per thread per iteration
+// (16-byte fp32 and 8-byte bf16 accesses). Skips the update (but still zeroes the
+// gradient) when the global norm in device memory is not finite.
+__global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, float* __restrict__ master,
+                                                    float* __restrict__ m, float* __restrict__ v,
+                                                    bf16* __restrict__ grad, int64_t n,
+                                                    const float* __restrict__ factor,
+                                                    const float* __restrict__ norm2, AdamHyper h) {
   const float norm = sqrtf(*norm2);
   const bool finite = isfinite(norm);
-  const float clip = finite ? fminf(1.f, max_norm / (norm + 1e-6f)) : 0.f;
+  const float clip = finite ? fminf(1.f, h.max_norm / (norm + 1e-6f)) : 0.f;
   const float fac = *factor;
-  const float decay = 1.f - lr * wd;
-  const float step = lr / bc1;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+  const float decay = 1.f - h.lr * h.wd;
+  const float step = h.lr / h.bc1;
+  const int64_t n4 = n / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float4* M4 = reinterpret_cast<float4*>(master);
+  float4* m4 = reinterpret_cast<float4*>(m);
+  float4* v4 = reinterpret_cast<float4*>(v);
+  uint2* g4 = reinterpret_cast<uint2*>(grad);
+  uint2* p4 = reinterpret_cast<uint2*>(param);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
     if (finite) {
-      const float g = r(f(grad[i]) * fac) * clip;
-      float mm = m[i];
-      mm = mm + (1.f - b1) * (g - mm);
-      const float vv = b2 * v[i] + (1.f - b2) * g * g;
-      const float denom = sqrtf(vv) / bc2 + eps;
-      const float w = master[i] * decay - step * (mm / denom);
+      const uint2 graw = g4[i];
+      const bf16* gh = reinterpret_cast<const bf16*>(&graw);
+      float4 W = M4[i], MM = m4[i], VV = v4[i];
+      float* w = reinterpret_cast<float*>(&W);
+      float* mm = reinterpret_cast<float*>(&MM);
+      float* vv = reinterpret_cast<float*>(&VV);
+      __nv_bfloat162 out[2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) adam_one(r(f(gh[j]) * fac) * clip, w[j], mm[j], vv[j], decay, step, h);
+      out[0] = __floats2bfloat162_rn(w[0], w[1]);
+      out[1] = __floats2bfloat162_rn(w[2], w[3]);
+      M4[i] = W;
+      m4[i] = MM;
+      v4[i] = VV;
+      p4[i] = *reinterpret_cast<uint2*>(out);
+    }
+    g4[i] = make_uint2(0u, 0u);
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    if (finite) {
+      float w = master[i], mm = m[i], vv = v[i];
+      adam_one(r(f(grad[i]) * fac) * clip, w, mm, vv, decay, step, h);
+      master[i] = w;
       m[i] = mm;
       v[i] = vv;
-      master[i] = w;
       param[i] = __float2bfloat16(w);
     }
     grad[i] = __float2bfloat16(0.f);
@@ -490,7 +542,8 @@ void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad) {
 
 void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2) {
   const int64_t n = grad.numel();
-  const int blocks = std::min<int64_t>(num_sms() * 4, std::max<int64_t>(1, (n + 255) / 256));
+  NS_CHECK(reinterpret_cast<uintptr_t>(grad.data_ptr()) % 16 == 0, "grad_norm_sq: 16-byte aligned shard expected");
+  const int blocks = (int)std::min<int64_t>(num_sms() * 4, std::max<int64_t>(1, (n / 8 + 255) / 256));
   auto part = at::empty({blocks}, grad.options().dtype(at::kFloat));
   grad_norm_part_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(grad.data_ptr()), n,
                                                       factor.data_ptr<float>(), part.data_ptr<float>());
@@ -503,11 +556,15 @@ void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor 
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
                   double bc1, double bc2, double max_norm) {
   const int64_t n = master.numel();
-  adamw_kernel<<<grid_for(n), 256, 0, stream()>>>(
-      reinterpret_cast<bf16*>(param.data_ptr()), master.data_ptr<float>(), m.data_ptr<float>(),
-      v.data_ptr<float>(), reinterpret_cast<bf16*>(grad.data_ptr()), n, factor.data_ptr<float>(),
-      norm2.data_ptr<float>(), (float)lr, (float)wd, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2,
-      (float)max_norm);
+  NS_CHECK(reinterpret_cast<uintptr_t>(master.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(grad.data_ptr()) % 8 == 0 &&
+               reinterpret_cast<uintptr_t>(param.data_ptr()) % 8 == 0,
+           "adamw: shard buffers must be 16/8-byte aligned");
+  AdamHyper h{(float)lr, (float)wd, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2, (float)max_norm};
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)num_sms() * 8));
+  adamw_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<bf16*>(param.data_ptr()), master.data_ptr<float>(),
+                                             m.data_ptr<float>(), v.data_ptr<float>(),
+                                             reinterpret_cast<bf16*>(grad.data_ptr()), n, factor.data_ptr<float>(),
+                                             norm2.data_ptr<float>(), h);
   NS_CUDA(cudaGetLastError());
 }
 

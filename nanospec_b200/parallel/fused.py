@@ -1,0 +1,187 @@
+"""Peer-memory sharding schedule: all-gather and reduce-scatter by our own kernels.
+
+Every training rank owns one *window* (a device allocation opened by all peers
+through CUDA IPC). The window holds this rank's parameter shard of every unit, two
+full-size gradient slots and a flag area; peers address it at the same offsets.
+
+* all-gather of unit i: a kernel on the communication stream pulls every rank's
+  shard straight out of the peers' windows over NVLink into a persistent local
+  buffer, one visit ahead of compute (the gathered weights stay resident for the
+  backward pass, so the model is gathered once per step);
+* reduce-scatter of unit i: after the backward of unit i writes its full gradient
+  into a window slot, each rank signals its peers, and every owner pulls its
+  shard-range of every peer's slot, sums the N contributions in fixed rank order,
+  averages and adds into its gradient shard (deterministic, NCCL AVG semantics);
+* synchronisation is by sequence-number flags in the windows (release stores /
+  acquire loads) with bounded waits: a peer that never signals makes the wait
+  kernel set the device error word and return, and the host raises.
+
+The protocol per step, all ranks in the same order:
+``begin``: barrier "parameters of step t final" (after the previous AdamW);
+``prefetch/acquire``: gather + event; ``gradient_buffer``: wait until every peer
+has pulled this slot's previous contents; ``reduce``: signal "slot ready", wait for
+all peers' "slot ready", pull-reduce, signal "slot pulled"; ``finish``: the
+compute stream waits for the communication stream.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import cuda_ops
+from .shard import ScheduleError
+
+FLAGS_BYTES = 4096
+CH_PARAMS, CH_PULLED, CH_READY = 0, 2, 4  # channels; PULLED/READY use +slot
+
+
+def _align(n, a=256):
+    return (n + a - 1) // a * a
+
+
+class PeerWindow:
+    """This rank's symmetric window and the peers' view of it."""
+
+    def __init__(self, plan, group=None):
+        self.C = cuda_ops()
+        first = plan.context
+        self.rank, self.world = first.rank, first.world_size
+        self.group = group if group is not None else first.group
+        units = list(plan)
+        off = FLAGS_BYTES
+        self.param_off = {}
+        for u in units:
+            self.param_off[id(u)] = off
+            off += _align(u.shard_size * 2)
+        self.slot_bytes = _align(max(u.full_size for u in units) * 2)
+        self.slot_off = [off, off + self.slot_bytes]
+        total = off + 2 * self.slot_bytes
+        self.id, _ = self.C.window_create(total, self.rank, self.world)
+        handle = self.C.window_ipc_handle(self.id)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.tolist(), group=self.group)
+        self.C.window_open(self.id, torch.tensor(handles, dtype=torch.uint8))
+        # Move every parameter shard into the window (values unchanged).
+        for u in units:
+            view = self.C.window_view(self.id, self.param_off[id(u)], u.shard_size, u.param.dtype)
+            view.copy_(u.param)
+            u.param = view
+        self.slots = [self.C.window_view(self.id, o, self.slot_bytes // 2, first.param.dtype)
+                      for o in self.slot_off]
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.C.window_close(self.id)
+
+
+class PeerSchedule:
+    """Resident gathered weights + window-slot gradient reduction (see module doc)."""
+
+    def __init__(self, plan, window: PeerWindow, timeout_s: float | None = None, serial=False):
+        """``serial=True`` runs every transfer on the compute stream (no overlap):
+        the same kernels in the same order, used as the bitwise reference."""
+        self.C = cuda_ops()
+        self.w = window
+        self.serial = serial
+        units = tuple(plan)
+        self.device = units[0].param.device
+        self.stream = torch.cuda.current_stream(self.device) if serial else torch.cuda.Stream(device=self.device)
+        self.resident = {id(u): torch.empty(u.full_size, device=self.device, dtype=u.param.dtype) for u in units}
+        self.ready = {id(u): torch.cuda.Event() for u in units}
+        self.reduced = [torch.cuda.Event(), torch.cuda.Event()]
+        self.seq = {CH_PARAMS: 0, CH_PULLED: 0, CH_PULLED + 1: 0, CH_READY: 0, CH_READY + 1: 0}
+        self.slot_owner = [None, None]
+        t = timeout_s if timeout_s is not None else float(os.environ.get("NANOSPEC_PEER_TIMEOUT_S", 60))
+        self.poll_limit = int(t / 200e-9)
+        self.active = False
+        self.visits = ()
+        self.gathered = set()
+
+    # ------------------------------------------------------------------ helpers
+    def _signal(self, channel):
+        self.seq[channel] += 1
+        self.C.peer_signal(self.w.id, 0, channel, self.seq[channel])
+
+    def _wait(self, channel, seq):
+        if seq > 0:
+            self.C.peer_wait(self.w.id, 0, channel, seq, self.poll_limit)
+
+    # ------------------------------------------------------------------ schedule API
+    def begin(self, visits):
+        if self.active:
+            raise ScheduleError("Finish the communication schedule before starting another")
+        self.visits = visits
+        self.compute = torch.cuda.current_stream(self.device)
+        if self.serial:
+            self.stream = self.compute
+        self.stream.wait_stream(self.compute)  # this rank's optimizer step is done
+        with torch.cuda.stream(self.stream):
+            self._signal(CH_PARAMS)
+            self._wait(CH_PARAMS, self.seq[CH_PARAMS])  # every peer's shards are final
+        self.gathered = set()
+        self.active = True
+
+    def prefetch(self, index):
+        if index >= len(self.visits):
+            return
+        unit = self.visits[index]
+        key = id(unit)
+        if key in self.gathered:
+            return
+        self.gathered.add(key)
+        with torch.cuda.stream(self.stream):
+            self.C.peer_allgather(self.w.id, self.w.param_off[key], unit.shard_size, self.resident[key])
+            self.ready[key].record(self.stream)
+
+    def acquire(self, index):
+        unit = self.visits[index]
+        key = id(unit)
+        if key not in self.gathered or unit.gathered is not None:
+            raise ScheduleError("Acquire exactly one prefetched unit")
+        self.compute.wait_event(self.ready[key])
+        unit.gathered = self.resident[key]
+        unit.bind(unit.gathered)
+        return unit
+
+    def gradient_buffer(self, index):
+        unit = self.visits[index]
+        slot = index % 2
+        if self.slot_owner[slot] is not None:
+            raise ScheduleError("gradient slot still bound")
+        # Every peer must have pulled this slot's previous contents.
+        self._wait(CH_PULLED + slot, self.seq[CH_PULLED + slot])
+        self.slot_owner[slot] = index
+        return self.w.slots[slot][:unit.full_size]
+
+    def release(self, index):
+        unit = self.visits[index]
+        unit.release()
+
+    def reduce(self, index):
+        unit = self.visits[index]
+        slot = index % 2
+        if self.slot_owner[slot] != index:
+            raise ScheduleError("reduce without a bound gradient slot")
+        self.slot_owner[slot] = None
+        unit.full_grad = None
+        self.release(index)
+        self._signal(CH_READY + slot)  # on compute: my slot holds unit's full gradient
+        seq = self.seq[CH_READY + slot]
+        self.stream.wait_stream(self.compute)
+        with torch.cuda.stream(self.stream):
+            self._wait(CH_READY + slot, seq)
+            self.C.peer_reduce_avg(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad)
+            self._signal(CH_PULLED + slot)
+
+    def finish(self):
+        self.compute.wait_stream(self.stream)
+        self.active = False
+
+    def close(self):
+        self.stream.synchronize()

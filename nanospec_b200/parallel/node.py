@@ -59,7 +59,7 @@ class Node:
             self.device = torch.device("cpu")
         if timeout_s is None:
             timeout_s = float(os.environ.get("NANOSPEC_PG_TIMEOUT", 600))
-        if not dist.is_initialized():
+        if not dist.is_initialized() and self.world > 1:
             kw = dict(timeout=timedelta(seconds=timeout_s))
             if backend == "nccl":
                 kw["device_id"] = self.device

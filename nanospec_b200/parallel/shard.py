@@ -191,14 +191,38 @@ class ShardingPlan:
         """
         return (self.context, *self.layers, self.heads, *self.layers[::-1], self.context)
 
+    def enable_peer(self, group=None, timeout_s=None):
+        """Switch this plan to peer-memory communication (``parallel.fused``).
+
+        Collective over the training ranks: moves every parameter shard into a
+        CUDA-IPC window that all ranks can address.
+        """
+        from .fused import PeerSchedule, PeerWindow
+        if "peer_window" in self._cache:
+            return
+        window = PeerWindow(self, group)
+        self._cache["peer_window"] = window
+        self._cache["peer"] = PeerSchedule(self, window, timeout_s)
+        self._cache["peer_serial"] = PeerSchedule(self, window, timeout_s, serial=True)
+
+    @property
+    def peer_enabled(self):
+        return "peer_window" in self._cache
+
     def schedule(self, sequence=None, *, overlap=True, resident=False):
         """A schedule over ``sequence`` (default: ``step_sequence()``).
 
-        ``overlap=False`` or one rank: ``SerialSchedule``. Otherwise the
-        double-buffered ``OverlapSchedule``, or ``ResidentSchedule`` when
-        ``resident`` (gathered weights kept from the forward for the backward).
+        With ``enable_peer``: the peer-memory schedule (overlapped, or serial on the
+        compute stream when ``overlap=False``). Otherwise ``overlap=False`` or one
+        rank: ``SerialSchedule``; else the double-buffered ``OverlapSchedule``, or
+        ``ResidentSchedule`` when ``resident`` (gathered weights kept from the
+        forward for the backward).
         """
         seq = tuple(self.step_sequence() if sequence is None else sequence)
+        if self.peer_enabled and self.context.world_size > 1:
+            sched = self._cache["peer" if overlap else "peer_serial"]
+            sched.begin(seq)
+            return sched
         on_cpu = self.context.param.device.type != "cuda"  # side streams exist on CUDA only
         if self.context.world_size == 1 or on_cpu or (not overlap and not resident):
             return SerialSchedule(seq)
@@ -211,9 +235,18 @@ class ShardingPlan:
         return sched
 
     def reset_pipeline(self):
+        if self.peer_enabled:
+            raise ScheduleError("a model whose shards live in a peer window cannot be moved")
         for sched in self._cache.values():
             sched.close()
         self._cache.clear()
+
+    def close_peer(self):
+        """Collective: release the peer window (after the last step)."""
+        if self.peer_enabled:
+            for key in ("peer", "peer_serial"):
+                self._cache.pop(key).close()
+            self._cache.pop("peer_window").close()
 
 
 class SerialSchedule:

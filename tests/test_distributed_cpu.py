@@ -27,7 +27,8 @@ def _worker(rank, world, port, fn, args, errq):
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world)
         fn(rank, world, *args)
-        dist.barrier()
+        if dist.is_initialized():
+            dist.barrier()
     except BaseException:  # report to the parent, never hang it
         errq.put((rank, traceback.format_exc()))
     finally:
@@ -187,3 +188,37 @@ def test_verifier_pipeline_handoff(world, train_gpus):
     with tempfile.TemporaryDirectory() as d:
         path = write_synthetic_checkpoint(os.path.join(d, "ck"), tiny_hybrid_text_config(), fp8=False, seed=2)
         run_ranks(world, _verifier, str(path), train_gpus, d)
+
+
+# ---------------------------------------------------------------------------- CLI
+def _cli(rank, world, outdir, extra):
+    from nanospec_b200.cli import main
+    rows = main(["--config", "tiny-hybrid", "--steps", "2", "--seq-len", "64", "--anchors", "4",
+                 "--dtype", "float32", "--output", os.path.join(outdir, "run.json"), "--backend", "gloo",
+                 "--learning-rate", "1e-3"] + extra)
+    if rank == 0:
+        assert len(rows) == 2 and all(r["updated"] for r in rows)
+
+
+def test_cli_with_synthetic_verifier_and_resume():
+    import glob
+    import json
+    with tempfile.TemporaryDirectory() as d:
+        run_ranks(2, _cli, d, ["--train-gpus", "1", "--synthetic-target", "tiny"])
+        report = json.load(open(os.path.join(d, "run.json")))
+        assert report["verifier"] and len(report["steps"]) == 2
+        ck = report["checkpoint"]
+        assert os.path.exists(os.path.join(ck, "metadata.json"))
+        run_ranks(2, _cli, d, ["--train-gpus", "1", "--synthetic-target", "tiny", "--checkpoint", ck])
+        report2 = json.load(open(os.path.join(d, "run.json")))
+        assert [r["step"] for r in report2["steps"]] == [3, 4]
+        assert len(glob.glob(os.path.join(d, "run-checkpoint-step*"))) == 2
+
+
+def test_cli_without_verifier_single_process():
+    with tempfile.TemporaryDirectory() as d:
+        from nanospec_b200.cli import main
+        os.environ.pop("WORLD_SIZE", None)
+        rows = main(["--config", "tiny", "--steps", "2", "--seq-len", "48", "--anchors", "4", "--dtype", "float32",
+                     "--output", os.path.join(d, "r.json"), "--no-verifier", "--backend", "gloo"])
+        assert len(rows) == 2

@@ -17,7 +17,7 @@ def C():
 
 
 def close(a, b, rtol=2e-2, atol=2e-2):
-    a, b = a.float(), b.float()
+    a, b = a.float().cpu(), b.float().cpu()
     err = (a - b).abs().max().item()
     scale = b.abs().max().item() + 1e-6
     cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()

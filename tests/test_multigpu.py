@@ -1,0 +1,156 @@
+"""Multi-GPU schedules on B200 (2+ GPUs; spawned NCCL ranks), plus the bounded-wait
+timeout of the peer flag protocol (1 GPU, a flag that nothing sets)."""
+
+import os
+import socket
+import tempfile
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import nanospec_b200 as N
+
+pytestmark = pytest.mark.gpu
+ngpu = torch.cuda.device_count() if torch.cuda.is_available() else 0
+two_gpus = pytest.mark.skipif(ngpu < 2, reason="needs 2 GPUs")
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, fn, args, errq):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        from datetime import timedelta
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        fn(rank, world, *args)
+        torch.cuda.synchronize()
+        dist.barrier()
+    except BaseException:
+        errq.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def run_ranks(world, fn, *args, timeout=600):
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fn, args, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not alive, "ranks timed out"
+    assert not errors, errors[0][1]
+
+
+def _model(rank, world, name="tiny-hybrid"):
+    c = N.DraftConfig.load(N.config_path(name))
+    g = torch.Generator().manual_seed(43)
+    emb = torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1
+    head = torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1
+    dev = torch.device("cuda", rank)
+    m = N.DSpark(c, N.initialize(c, 42, torch.bfloat16), emb, head, device=dev, dtype=torch.bfloat16,
+                 group=dist.group.WORLD, world_size=world, rank=rank)
+    return c, m
+
+
+def _data(c, rank, b=8, s=512):
+    dev = torch.device("cuda", rank)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    ids = torch.randint(0, c.vocab_size, (b, s), device=dev, generator=g)
+    hs = [torch.randn(b, s, c.hidden_size, device=dev, generator=g).bfloat16() for _ in range(c.num_target_layers)]
+    last = torch.randn(b, s, c.hidden_size, device=dev, generator=g).bfloat16()
+    mask = torch.ones(b, s, device=dev)
+    if rank % 2:
+        mask[:, 100:103] = 0
+    return ids, hs, last, mask
+
+
+def _digest(m):
+    return [t.clone() for s in m.sharding for t in (s.param, s.master, s.m, s.v)]
+
+
+def _schedules(rank, world, outdir):
+    c, m = _model(rank, world)
+    o = N.Objective(num_anchors=8)
+    ids, hs, last, mask = _data(c, rank)
+    init = [s.param.clone() for s in m.sharding]
+    results = {}
+    for mode in ("nccl_serial", "nccl_overlap", "peer_serial", "peer_overlap"):
+        if mode.startswith("peer"):
+            m.sharding.enable_peer()
+        for s, p0 in zip(m.sharding, init):
+            s.param.copy_(p0)
+            s.master.copy_(s.param)
+            s.m.zero_(), s.v.zero_(), s.grad.zero_()
+        opt = N.AdamW(m.sharding, lr=1e-3, weight_decay=0.01)
+        rows = []
+        for _ in range(3):
+            torch.manual_seed(7 + rank)
+            r = N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last), loss_mask=mask, optimizer=opt,
+                        overlap=mode.endswith("overlap"))
+            rows.append((r.metrics.loss.item(), r.update["grad_norm"], r.hidden.clone()))
+        results[mode] = (rows, _digest(m))
+    m.sharding.close_peer()
+    a, b = results["peer_serial"], results["peer_overlap"]
+    for ra, rb in zip(a[0], b[0]):
+        assert ra[0] == rb[0] and ra[1] == rb[1] and torch.equal(ra[2], rb[2])
+    for x, y in zip(a[1], b[1]):
+        assert torch.equal(x, y), "peer serial vs overlap must be bitwise equal"
+    a, b = results["nccl_serial"], results["nccl_overlap"]
+    for x, y in zip(a[1], b[1]):
+        assert torch.equal(x, y), "NCCL serial vs overlap must be bitwise equal"
+    # peer vs NCCL: same math, different reduction order
+    for ra, rb in zip(results["nccl_serial"][0], results["peer_serial"][0]):
+        assert abs(ra[0] - rb[0]) <= 1e-3 * abs(ra[0])
+    for x, y in zip(results["nccl_serial"][1], results["peer_serial"][1]):
+        rel = ((x.float() - y.float()).norm() / x.float().norm().clamp_min(1e-12)).item()
+        assert rel < 3e-3, rel
+
+
+@two_gpus
+def test_schedules_bitwise_and_peer_matches_nccl():
+    with tempfile.TemporaryDirectory() as d:
+        run_ranks(2, _schedules, d)
+
+
+@pytest.mark.skipif(ngpu < 4, reason="needs 4 GPUs")
+def test_schedules_four_ranks():
+    with tempfile.TemporaryDirectory() as d:
+        run_ranks(4, _schedules, d)
+
+
+@pytest.mark.skipif(ngpu < 1, reason="needs a GPU")
+def test_peer_wait_times_out_without_hanging():
+    """A wait on a flag that no rank ever sets returns with an error status."""
+    from nanospec_b200.ops._ext import cuda_ops
+    C = cuda_ops()
+    C.clear_device_error()
+    wid, _ = C.window_create(1 << 20, 0, 1)
+    C.window_open(wid, C.window_ipc_handle(wid).view(1, -1))
+    C.peer_wait(wid, 0, 5, 1, 2000)  # ~0.4 ms of polling, then give up
+    torch.cuda.synchronize()
+    assert C.device_error() == 2
+    C.clear_device_error()
+    # the context stays usable
+    x = torch.ones(4, device="cuda")
+    assert (x + 1).sum().item() == 8
+    C.window_close(wid)
