@@ -52,10 +52,13 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // Ring depth chosen so two CTAs fit on one SM (228 KB of shared memory).
+  // Ring depth: two CTAs per SM when the grid has more CTAs than SMs (epilogues
+  // overlap mainloops); otherwise one CTA per SM with the deepest ring that fits,
+  // so weight-streaming products keep ~200 KB of loads in flight per SM.
   static constexpr int STAGES = (110 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES_SOLO = (224 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  static constexpr int SMEM_MAX = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_MAX = STAGES_SOLO * STAGE_BYTES + 1024 + 256;
 };
 
 __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, float acc) {
@@ -313,12 +316,12 @@ static int pick_bn(int N) {
   return 256;
 }
 
-static int max_stages(int bn) {
+static int max_stages(int bn, bool solo) {
   switch (bn) {
-    case 64: return GemmCfg<64>::STAGES;
-    case 128: return GemmCfg<128>::STAGES;
-    case 192: return GemmCfg<192>::STAGES;
-    default: return GemmCfg<256>::STAGES;
+    case 64: return solo ? GemmCfg<64>::STAGES_SOLO : GemmCfg<64>::STAGES;
+    case 128: return solo ? GemmCfg<128>::STAGES_SOLO : GemmCfg<128>::STAGES;
+    case 192: return solo ? GemmCfg<192>::STAGES_SOLO : GemmCfg<192>::STAGES;
+    default: return solo ? GemmCfg<256>::STAGES_SOLO : GemmCfg<256>::STAGES;
   }
 }
 
@@ -363,7 +366,8 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   }
   int kpb = (kb + splits - 1) / splits;
   splits = (kb + kpb - 1) / kpb;
-  const int stages = std::max(1, std::min(max_stages(bn), kpb));
+  const bool solo = (int64_t)tiles * splits <= num_sms();
+  const int stages = std::max(1, std::min(max_stages(bn, solo), kpb));
 
   GemmArgs a{};
   a.M = M;

@@ -358,25 +358,46 @@ __global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, fl
   float4* v4 = reinterpret_cast<float4*>(v);
   uint2* g4 = reinterpret_cast<uint2*>(grad);
   uint2* p4 = reinterpret_cast<uint2*>(param);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+  // Two groups of 4 per iteration: all ten loads are issued before any arithmetic.
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n4; i0 += 2 * stride) {
+    const int64_t i1 = i0 + stride;
+    const bool has1 = i1 < n4;
     if (finite) {
-      const uint2 graw = g4[i];
-      const bf16* gh = reinterpret_cast<const bf16*>(&graw);
-      float4 W = M4[i], MM = m4[i], VV = v4[i];
-      float* w = reinterpret_cast<float*>(&W);
-      float* mm = reinterpret_cast<float*>(&MM);
-      float* vv = reinterpret_cast<float*>(&VV);
-      __nv_bfloat162 out[2];
+      uint2 graw[2];
+      float4 W[2], MM[2], VV[2];
+      graw[0] = __ldcs(g4 + i0);
+      W[0] = __ldcs(M4 + i0);
+      MM[0] = __ldcs(m4 + i0);
+      VV[0] = __ldcs(v4 + i0);
+      if (has1) {
+        graw[1] = __ldcs(g4 + i1);
+        W[1] = __ldcs(M4 + i1);
+        MM[1] = __ldcs(m4 + i1);
+        VV[1] = __ldcs(v4 + i1);
+      }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) adam_one(r(f(gh[j]) * fac) * clip, w[j], mm[j], vv[j], decay, step, h);
-      out[0] = __floats2bfloat162_rn(w[0], w[1]);
-      out[1] = __floats2bfloat162_rn(w[2], w[3]);
-      M4[i] = W;
-      m4[i] = MM;
-      v4[i] = VV;
-      p4[i] = *reinterpret_cast<uint2*>(out);
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && !has1) break;
+        const int64_t i = u ? i1 : i0;
+        const bf16* gh = reinterpret_cast<const bf16*>(&graw[u]);
+        float* w = reinterpret_cast<float*>(&W[u]);
+        float* mm = reinterpret_cast<float*>(&MM[u]);
+        float* vv = reinterpret_cast<float*>(&VV[u]);
+        __nv_bfloat162 out[2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) adam_one(r(f(gh[j]) * fac) * clip, w[j], mm[j], vv[j], decay, step, h);
+        out[0] = __floats2bfloat162_rn(w[0], w[1]);
+        out[1] = __floats2bfloat162_rn(w[2], w[3]);
+        __stcs(M4 + i, W[u]);
+        __stcs(m4 + i, MM[u]);
+        __stcs(v4 + i, VV[u]);
+        __stcs(p4 + i, *reinterpret_cast<uint2*>(out));
+        __stcs(g4 + i, make_uint2(0u, 0u));
+      }
+    } else {
+      g4[i0] = make_uint2(0u, 0u);
+      if (has1) g4[i1] = make_uint2(0u, 0u);
     }
-    g4[i] = make_uint2(0u, 0u);
   }
   for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     if (finite) {

@@ -14,7 +14,7 @@ import torch
 
 from ._ext import cuda_ops
 
-VOCAB_CHUNK = int(os.environ.get("NANOSPEC_VOCAB_CHUNK", 8192))
+VOCAB_CHUNK = int(os.environ.get("NANOSPEC_VOCAB_CHUNK", 16384))
 
 
 def head_loss_cuda(hidden, lm_head, markov_e, markov_w2, prepared, o, *, target_hidden=None,

@@ -71,6 +71,9 @@ class PeerWindow:
             u.param = view
         self.slots = [self.C.window_view(self.id, o, self.slot_bytes // 2, first.param.dtype)
                       for o in self.slot_off]
+        # Flag sequence numbers belong to the window: every schedule using it (the
+        # overlapped and the serial one) continues the same monotonic sequences.
+        self.seq = {CH_PARAMS: 0, CH_PULLED: 0, CH_PULLED + 1: 0, CH_READY: 0, CH_READY + 1: 0}
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
 
@@ -95,7 +98,7 @@ class PeerSchedule:
         self.resident = {id(u): torch.empty(u.full_size, device=self.device, dtype=u.param.dtype) for u in units}
         self.ready = {id(u): torch.cuda.Event() for u in units}
         self.reduced = [torch.cuda.Event(), torch.cuda.Event()]
-        self.seq = {CH_PARAMS: 0, CH_PULLED: 0, CH_PULLED + 1: 0, CH_READY: 0, CH_READY + 1: 0}
+        self.seq = window.seq
         self.slot_owner = [None, None]
         t = timeout_s if timeout_s is not None else float(os.environ.get("NANOSPEC_PEER_TIMEOUT_S", 60))
         self.poll_limit = int(t / 200e-9)

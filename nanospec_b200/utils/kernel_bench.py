@@ -1,0 +1,163 @@
+"""Microbenchmarks of single hot ops on one GPU (CUDA-event timing, JSON lines).
+
+    python -m nanospec_b200.utils.kernel_bench gemm --kind fwd --T 56 --nout 5120 --k 5120
+    python -m nanospec_b200.utils.kernel_bench adamw --n 300000000
+    python -m nanospec_b200.utils.kernel_bench head --T 56 --hidden 5120 --vocab 248320
+    python -m nanospec_b200.utils.kernel_bench attention --S 128 --blocks 8
+    python -m nanospec_b200.utils.kernel_bench fp8 --T 4096 --k 5120 --nout 17408
+    python -m nanospec_b200.utils.kernel_bench gdn --S 4096 --heads 48
+
+Each run does ``--warmup`` untimed calls, then times ``--reps`` calls between two
+events on the launching stream. Operands rotate through enough copies to exceed
+the 126 MB L2 when ``--rotate`` is set, so every call streams from HBM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def _time(fn, reps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1000.0 / reps  # microseconds
+
+
+def _copies(make, bytes_each, rotate):
+    n = max(1, (160 << 20) // max(1, bytes_each)) if rotate else 1
+    return [make() for _ in range(min(n, 16))]
+
+
+def bench_gemm(a):
+    from nanospec_b200 import ops
+    dev = "cuda"
+    ws = _copies(lambda: (torch.randn(a.nout, a.k, device=dev) * 0.02).bfloat16(), a.nout * a.k * 2, a.rotate)
+    x = torch.randn(a.T, a.k, device=dev).bfloat16()
+    dy = torch.randn(a.T, a.nout, device=dev).bfloat16()
+    y = torch.empty(a.T, a.nout, device=dev).bfloat16()
+    dx = torch.empty(a.T, a.k, device=dev).bfloat16()
+    dw = torch.empty(a.nout, a.k, device=dev).bfloat16()
+    it = [0]
+
+    def w():
+        it[0] = (it[0] + 1) % len(ws)
+        return ws[it[0]]
+    fn = {"fwd": lambda: ops.linear(x, w(), out=y),
+          "dgrad": lambda: ops.linear_dgrad(dy, w(), out=dx),
+          "wgrad": lambda: ops.linear_wgrad(dy, x, dw)}[a.kind]
+    us = _time(fn, a.reps, a.warmup)
+    flops = 2.0 * a.T * a.nout * a.k
+    wbytes = a.nout * a.k * 2
+    return {"op": f"gemm_{a.kind}", "T": a.T, "nout": a.nout, "k": a.k, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "weight_TBps": round(wbytes / us / 1e6, 3)}
+
+
+def bench_adamw(a):
+    from nanospec_b200.ops._ext import cuda_ops
+    C = cuda_ops()
+    n = a.n
+    p = torch.zeros(n, device="cuda").bfloat16()
+    g = torch.zeros(n, device="cuda").bfloat16()
+    m32, mm, vv = (torch.zeros(n, device="cuda") for _ in range(3))
+    f = torch.ones(1, device="cuda")
+    n2 = torch.ones(1, device="cuda")
+    us = _time(lambda: C.adamw_update(p, m32, mm, vv, g, f, n2, 1e-5, 0.01, 0.9, 0.999, 1e-8, 0.1, 0.03, 1.0),
+               a.reps, a.warmup)
+    return {"op": "adamw", "n": n, "us": round(us, 1), "TBps": round(26.0 * n / us / 1e6, 3)}
+
+
+def bench_head(a):
+    import nanospec_b200 as N
+    from nanospec_b200.objective import head_loss
+    dev = "cuda"
+    o = N.Objective(num_anchors=a.T // 7)
+    ids = torch.randint(0, a.vocab, (1, 4 * a.T), device=dev)
+    prep = N.prepare(ids, torch.ones(1, 4 * a.T, device=dev), o)
+    t = prep.weights.numel()
+    h = (torch.randn(t, a.hidden, device=dev) * 0.3).bfloat16()
+    th = (torch.randn(t, a.hidden, device=dev) * 0.3).bfloat16()
+    W = (torch.randn(a.vocab, a.hidden, device=dev) * 0.02).bfloat16()
+    e = (torch.randn(t, a.rank, device=dev) * 0.3).bfloat16()
+    w2 = (torch.randn(a.vocab, a.rank, device=dev) * 0.02).bfloat16()
+    dw2 = torch.empty_like(w2)
+    us = _time(lambda: head_loss(h, W, e, w2, prep, o, target_hidden=th, dw2_out=dw2), a.reps, a.warmup)
+    flops = 2.0 * t * a.vocab * (2 * (a.hidden + a.rank) + a.hidden + a.hidden + 2 * a.rank)
+    return {"op": "ce_kl_head", "tokens": t, "vocab": a.vocab, "us": round(us, 1),
+            "tflops": round(flops / us / 1e6, 1), "lm_head_reads_TBps": round(2 * W.numel() * 2 / us / 1e6, 3)}
+
+
+def bench_attention(a):
+    from nanospec_b200 import ops
+    dev = "cuda"
+    b, S, nb, bs, hq, hk, d = 1, a.S, a.blocks, 7, 40, 8, 128
+    td = nb * bs
+    q = torch.randn(b, td, hq, d, device=dev).bfloat16()
+    kv = torch.randn(b * (S + td), 2 * hk * d, device=dev).bfloat16()
+    k, v = kv[:, :hk * d].view(-1, hk, d), kv[:, hk * d:].view(-1, hk, d)
+    anchors = torch.sort(torch.randint(0, S - bs, (b, nb), device=dev)).values
+    keep = torch.ones(b, nb, dtype=torch.bool, device=dev)
+    out, lse = ops.attention(q, k, v, anchors, keep, S, bs)
+    dout = torch.randn_like(q)
+    f_us = _time(lambda: ops.attention(q, k, v, anchors, keep, S, bs), a.reps, a.warmup)
+    b_us = _time(lambda: ops.attention_backward(dout, q, k, v, out, lse, anchors, keep, S, bs), a.reps, a.warmup)
+    return {"op": "draft_attention", "S": S, "blocks": nb, "fwd_us": round(f_us, 1), "bwd_us": round(b_us, 1)}
+
+
+def bench_fp8(a):
+    from nanospec_b200.models.verifier import quantize_weight_blocks
+    from nanospec_b200.ops import verifier_ops as vops
+    w, s = quantize_weight_blocks(torch.randn(a.nout, a.k) * 0.02)
+    w, s = w.cuda(), s.cuda()
+    x = torch.randn(a.T, a.k, device="cuda").bfloat16()
+    us = _time(lambda: vops.fp8_linear(x, w, s), a.reps, a.warmup)
+    return {"op": "fp8_linear", "T": a.T, "nout": a.nout, "k": a.k, "us": round(us, 1),
+            "tflops": round(2.0 * a.T * a.nout * a.k / us / 1e6, 1)}
+
+
+def bench_gdn(a):
+    from nanospec_b200.ops import verifier_ops as vops
+    b, s, nk, nv, d = 1, a.S, a.heads // 3, a.heads, 128
+    q = torch.randn(b, s, nk, d, device="cuda").bfloat16()
+    k = torch.randn(b, s, nk, d, device="cuda").bfloat16()
+    v = torch.randn(b, s, nv, d, device="cuda").bfloat16()
+    g = -torch.rand(b, s, nv, device="cuda") * 0.1
+    beta = torch.rand(b, s, nv, device="cuda").bfloat16()
+    us = _time(lambda: vops.gated_delta_rule(q, k, v, g, beta, nv // nk), a.reps, a.warmup)
+    return {"op": "gdn_chunk_fwd", "S": s, "heads": nv, "us": round(us, 1)}
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn"))
+    p.add_argument("--kind", choices=("fwd", "dgrad", "wgrad"), default="fwd")
+    p.add_argument("--T", type=int, default=56)
+    p.add_argument("--nout", type=int, default=5120)
+    p.add_argument("--k", type=int, default=5120)
+    p.add_argument("--n", type=int, default=300_000_000)
+    p.add_argument("--hidden", type=int, default=5120)
+    p.add_argument("--vocab", type=int, default=248320)
+    p.add_argument("--rank", type=int, default=256)
+    p.add_argument("--S", type=int, default=128)
+    p.add_argument("--blocks", type=int, default=8)
+    p.add_argument("--heads", type=int, default=48)
+    p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--rotate", action="store_true", help="rotate operands through > L2 bytes")
+    a = p.parse_args(argv)
+    fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
+          "fp8": bench_fp8, "gdn": bench_gdn}[a.op]
+    print(json.dumps(fn(a)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
