@@ -24,7 +24,8 @@ void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad);
 void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2);
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
-                  double bc1, double bc2, double max_norm);
+                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev);
+void adam_prepare(at::Tensor norm2, at::Tensor step, double b1, double b2, at::Tensor bc);
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
               at::Tensor out, at::Tensor lse);
 void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
@@ -53,6 +54,8 @@ void peer_allgather(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor ou
 void peer_reduce_avg(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad);
 void peer_signal(int64_t id, int64_t flags_off, int64_t channel, int64_t seq);
 void peer_wait(int64_t id, int64_t flags_off, int64_t channel, int64_t seq, int64_t poll_limit);
+std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
+                                      at::Tensor dout, int64_t groups);
 int64_t device_error();
 void clear_device_error();
 }  // namespace ns
@@ -72,7 +75,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &ns::embedding_fwd);
   m.def("embedding_bwd", &ns::embedding_bwd);
   m.def("grad_norm_sq", &ns::grad_norm_sq);
-  m.def("adamw_update", &ns::adamw_update);
+  m.def("adamw_update", &ns::adamw_update, py::arg("param"), py::arg("master"), py::arg("m"), py::arg("v"),
+        py::arg("grad"), py::arg("factor"), py::arg("norm2"), py::arg("lr"), py::arg("wd"), py::arg("b1"),
+        py::arg("b2"), py::arg("eps"), py::arg("bc1"), py::arg("bc2"), py::arg("max_norm"),
+        py::arg("bc_dev") = py::none());
+  m.def("adam_prepare", &ns::adam_prepare);
   m.def("attn_fwd", &ns::attn_fwd);
   m.def("attn_bwd", &ns::attn_bwd);
   m.def("head_loss", &ns::head_loss);
@@ -94,6 +101,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_reduce_avg", &ns::peer_reduce_avg);
   m.def("peer_signal", &ns::peer_signal);
   m.def("peer_wait", &ns::peer_wait);
+  m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
   m.def("clear_device_error", &ns::clear_device_error);
 }

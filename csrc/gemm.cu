@@ -291,9 +291,10 @@ static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_MAX));
     attr = true;
   }
-  // TMEM holds 512 columns per SM: reserve enough shared memory that no more CTAs
-  // co-reside than their accumulators fit (an allocation never has to wait).
-  const int min_smem = (228 * 1024) / (512 / C::TMEM_COLS) - 1024 + 1;
+  // TMEM holds 512 columns per SM: reserve enough shared memory that no more than
+  // k = 512 / TMEM_COLS CTAs co-reside (an allocation never has to wait), i.e. k+1
+  // CTAs (each also pays 1 KB of reserved shared memory) must not fit in 228 KB.
+  const int min_smem = (228 * 1024) / (512 / C::TMEM_COLS + 1) - 1024 + 64;
   const int smem = std::max(stages * C::STAGE_BYTES + 1024 + 256, std::min(min_smem, C::SMEM_MAX));
   kern<<<grid, 192, smem, stream()>>>(ta, tb, a, stages);
   NS_CUDA(cudaGetLastError());

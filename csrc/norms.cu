@@ -326,7 +326,21 @@ __global__ void sum_into_kernel(const float* __restrict__ part, int parts, float
 
 struct AdamHyper {
   float lr, wd, b1, b2, eps, bc1, bc2, max_norm;
+  const float* bc;  // when set: device-resident {bc1, bc2} (overrides the fields above)
 };
+
+// Device-side step bookkeeping: if the global norm is finite, step += 1; then the
+// bias corrections of the (new) step, in double precision: bc = {1 - b1^t, sqrt(1 - b2^t)}.
+__global__ void adam_prepare_kernel(const float* __restrict__ norm2, long long* __restrict__ step, double b1,
+                                    double b2, float* __restrict__ bc) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const bool finite = isfinite(sqrtf(*norm2));
+  const long long t = *step + (finite ? 1 : 0);
+  if (finite) *step = t;
+  const double tt = (double)(t > 0 ? t : 1);
+  bc[0] = (float)(1.0 - pow(b1, tt));
+  bc[1] = (float)sqrt(1.0 - pow(b2, tt));
+}
 
 __device__ __forceinline__ void adam_one(float g, float& w, float& mm, float& vv, float decay, float step,
                                          const AdamHyper& h) {
@@ -350,6 +364,10 @@ __global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, fl
   const float clip = finite ? fminf(1.f, h.max_norm / (norm + 1e-6f)) : 0.f;
   const float fac = *factor;
   const float decay = 1.f - h.lr * h.wd;
+  if (h.bc) {
+    h.bc1 = h.bc[0];
+    h.bc2 = h.bc[1];
+  }
   const float step = h.lr / h.bc1;
   const int64_t n4 = n / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -575,17 +593,24 @@ void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2) {
 
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
-                  double bc1, double bc2, double max_norm) {
+                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev) {
   const int64_t n = master.numel();
   NS_CHECK(reinterpret_cast<uintptr_t>(master.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(grad.data_ptr()) % 8 == 0 &&
                reinterpret_cast<uintptr_t>(param.data_ptr()) % 8 == 0,
            "adamw: shard buffers must be 16/8-byte aligned");
-  AdamHyper h{(float)lr, (float)wd, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2, (float)max_norm};
+  AdamHyper h{(float)lr, (float)wd, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2, (float)max_norm,
+              bc_dev && bc_dev->defined() ? bc_dev->data_ptr<float>() : nullptr};
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)num_sms() * 8));
   adamw_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<bf16*>(param.data_ptr()), master.data_ptr<float>(),
                                              m.data_ptr<float>(), v.data_ptr<float>(),
                                              reinterpret_cast<bf16*>(grad.data_ptr()), n, factor.data_ptr<float>(),
                                              norm2.data_ptr<float>(), h);
+  NS_CUDA(cudaGetLastError());
+}
+
+void adam_prepare(at::Tensor norm2, at::Tensor step, double b1, double b2, at::Tensor bc) {
+  NS_CHECK(step.scalar_type() == at::kLong && bc.scalar_type() == at::kFloat && bc.numel() >= 2, "adam_prepare: types");
+  adam_prepare_kernel<<<1, 32, 0, stream()>>>(norm2.data_ptr<float>(), step.data_ptr<int64_t>() ? reinterpret_cast<long long*>(step.data_ptr<int64_t>()) : nullptr, b1, b2, bc.data_ptr<float>());
   NS_CUDA(cudaGetLastError());
 }
 

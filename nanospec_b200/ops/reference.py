@@ -342,3 +342,16 @@ def partial_rope(x, cos, sin, rotary_dim):
     """RoPE on the first ``rotary_dim`` channels of each head. x [b, s, H, D]; cos/sin [b, s, rd]."""
     c, s_ = cos.unsqueeze(2), sin.unsqueeze(2)
     return torch.cat((rope(x[..., :rotary_dim], c, s_), x[..., rotary_dim:]), -1)
+
+
+def gated_delta_rule_backward(q, k, v, g, beta, dout):
+    """Gradients (dq, dk, dv, dg, dbeta) of ``gated_delta_rule_recurrent`` by autograd in fp32.
+
+    The verifier is frozen, so training never needs this; it is the oracle of the
+    backward kernel (q, k are the raw, pre-normalisation inputs).
+    """
+    with torch.enable_grad():
+        leaves = [t.detach().float().requires_grad_(True) for t in (q, k, v, g, beta)]
+        out = gated_delta_rule_recurrent(*leaves)
+        out.backward(dout.float())
+    return tuple(t.grad for t in leaves)

@@ -133,3 +133,24 @@ def causal_attention_gated(q, k, v, gate, cos, sin, rotary_dim):
     k = ref.partial_rope(k, cos, sin, rotary_dim)
     o = ref.causal_attention(q, k, v)
     return o * gate.sigmoid()
+
+
+def gated_delta_rule_backward(q, k, v, g, beta, dout, groups=1):
+    """Gradients (dq, dk, dv, dg, dbeta) of the gated delta rule w.r.t. its raw inputs.
+
+    Not needed to train the draft (the verifier is frozen); provided as an op with a
+    hand-written backward for completeness and benchmarking.
+    """
+    if q.is_cuda:
+        return tuple(_c().gdn_chunk_bwd(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
+                                        beta.contiguous(), dout.contiguous(), int(groups)))
+    if groups > 1:
+        qr, kr = q.repeat_interleave(groups, 2), k.repeat_interleave(groups, 2)
+    else:
+        qr, kr = q, k
+    dq, dk, dv, dg, db = ref.gated_delta_rule_backward(qr, kr, v, g, beta, dout)
+    if groups > 1:
+        b, s, nv, d = dq.shape
+        dq = dq.view(b, s, nv // groups, groups, d).sum(3)
+        dk = dk.view(b, s, nv // groups, groups, d).sum(3)
+    return dq, dk, dv, dg, db

@@ -29,11 +29,34 @@ from ..ops._ext import cuda_ops
 
 
 class AdamW:
+    """Hyper-parameters and step count of the sharded optimizer (state lives in the shards).
+
+    On CUDA the step count is kept on the device (it only advances on finite updates,
+    which the device decides); ``steps`` reads it back on demand. ``sync=False`` makes
+    ``adamw_step`` return 0-dim device tensors instead of Python floats, so a training
+    loop never waits for the GPU between steps.
+    """
+
     def __init__(self, shards, lr=6e-4, weight_decay=0.0, betas=(0.9, 0.999), eps=1e-8,
-                 max_grad_norm=1.0):
+                 max_grad_norm=1.0, sync=True):
         self.shards = list(shards)
         self.lr, self.weight_decay, self.betas = lr, weight_decay, tuple(betas)
-        self.eps, self.max_grad_norm, self.steps = eps, max_grad_norm, 0
+        self.eps, self.max_grad_norm = eps, max_grad_norm
+        self.sync = sync
+        self._steps = 0
+        self._dev_step = None
+
+    @property
+    def steps(self):
+        if self._dev_step is not None:
+            return int(self._dev_step.item())
+        return self._steps
+
+    @steps.setter
+    def steps(self, value):
+        self._steps = int(value)
+        if self._dev_step is not None:
+            self._dev_step.fill_(int(value))
 
 
 def zero_grad(optimizer):
@@ -82,17 +105,18 @@ def _adamw_cuda(optimizer, den, factor, b1, b2):
         C.grad_norm_sq(s.grad, f, norm2)
     if first.world_size > 1:
         dist.all_reduce(norm2, group=first.group)
-    step = optimizer.steps + 1
-    bc1 = 1.0 - b1 ** step
-    bc2 = math.sqrt(1.0 - b2 ** step)
+    if optimizer._dev_step is None:
+        optimizer._dev_step = torch.tensor([optimizer._steps], dtype=torch.int64, device=den.device)
+        optimizer._bc = torch.empty(2, dtype=torch.float32, device=den.device)
+    # On the device: advance the step if the norm is finite, form the bias corrections.
+    C.adam_prepare(norm2, optimizer._dev_step, float(b1), float(b2), optimizer._bc)
     for s in optimizer.shards:
         C.adamw_update(s.param, s.master, s.m, s.v, s.grad, f, norm2, float(optimizer.lr),
                        float(optimizer.weight_decay), float(b1), float(b2), float(optimizer.eps),
-                       float(bc1), float(bc2), float(optimizer.max_grad_norm))
+                       1.0, 1.0, float(optimizer.max_grad_norm), optimizer._bc)
         s.grad_zero = True
-    norm = norm2.sqrt()
-    vals = torch.stack((norm.reshape(()), den.reshape(()))).tolist()
-    finite = math.isfinite(vals[0])
-    if finite:
-        optimizer.steps = step
-    return {"grad_norm": vals[0], "updated": finite, "denominator": vals[1]}
+    norm = norm2.sqrt().reshape(())
+    if not optimizer.sync:
+        return {"grad_norm": norm, "updated": torch.isfinite(norm), "denominator": den.reshape(())}
+    vals = torch.stack((norm, den.reshape(()))).tolist()
+    return {"grad_norm": vals[0], "updated": math.isfinite(vals[0]), "denominator": vals[1]}

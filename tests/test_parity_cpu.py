@@ -85,3 +85,24 @@ def test_teacher_logits_path_matches(reference):
                                loss_mask=mask)
     assert abs(r.metrics.loss.item() - rr.metrics.loss.item()) < 1e-5
     assert torch.allclose(r.hidden, rr.hidden, atol=1e-5)
+
+
+def test_gdn_backward_oracle_matches_finite_differences():
+    from nanospec_b200.ops import reference as R
+    torch.manual_seed(0)
+    b, s, h, d = 1, 9, 1, 4
+    args = [torch.randn(b, s, h, d, dtype=torch.float64) for _ in range(3)]
+    args += [-torch.rand(b, s, h, dtype=torch.float64), torch.rand(b, s, h, dtype=torch.float64)]
+    w = torch.randn(b, s, h, d, dtype=torch.float64)
+    grads = R.gated_delta_rule_backward(*args, w)
+    eps = 1e-3
+    for which in range(5):
+        x = args[which]
+        idx = (0, 3) + ((0, 1) if x.dim() == 4 else (0,))
+        plus = [a.clone() for a in args]
+        minus = [a.clone() for a in args]
+        plus[which][idx] += eps
+        minus[which][idx] -= eps
+        f = lambda a: (R.gated_delta_rule_recurrent(*[t.float() for t in a]).double() * w).sum()  # noqa: E731
+        fd = (f(plus) - f(minus)) / (2 * eps)
+        assert abs(fd.item() - grads[which][idx].item()) < 2e-2 * max(1.0, abs(fd.item()))

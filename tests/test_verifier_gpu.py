@@ -106,3 +106,20 @@ def test_stage_forward_matches_cpu(tmp_path):
     close(outs["cuda"][0], outs["cpu"][0], rtol=5e-2, cos_min=0.995)
     for i in (1, 3):
         close(outs["cuda"][1][i], outs["cpu"][1][i], rtol=5e-2, cos_min=0.995)
+
+
+@cuda
+@pytest.mark.parametrize("D,s,groups", [(16, 70, 2), (128, 130, 3)])
+def test_gated_delta_rule_backward(D, s, groups):
+    b, nk = 1, 2
+    nv = nk * groups
+    q = torch.randn(b, s, nk, D).bfloat16()
+    k = torch.randn(b, s, nk, D).bfloat16()
+    v = torch.randn(b, s, nv, D).bfloat16()
+    g = -torch.rand(b, s, nv) * 0.5
+    beta = torch.rand(b, s, nv).bfloat16()
+    dout = torch.randn(b, s, nv, D).bfloat16()
+    expect = vops.gated_delta_rule_backward(q, k, v, g, beta, dout, groups)
+    got = vops.gated_delta_rule_backward(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), dout.cuda(), groups)
+    for name, x, y in zip(("dq", "dk", "dv", "dg", "dbeta"), got, expect):
+        close(x, y, rtol=3e-2, cos_min=0.999)
