@@ -49,6 +49,7 @@ def parse():
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="one rank: run eagerly, not as a CUDA graph")
     p.add_argument("--comm", choices=("peer", "nccl"), default="peer",
                    help="N>1: peer-memory kernels over NVLink (default) or NCCL collectives")
     return p.parse_args()
@@ -204,7 +205,16 @@ def main():
     ids, states, last, mask = synthetic_batch(c, args.seq_len, rank, args.seed, dev, dtype)
     batch = TB(states, last)
 
+    graphed = None
+    if args.impl == "ours" and world == 1 and not args.no_graph:
+        # Single rank: the whole step (fwd, head, bwd, AdamW) replays as one CUDA graph.
+        from nanospec_b200.graphs import GraphedStep
+        torch.manual_seed(args.seed + rank)
+        graphed = GraphedStep(model, o, opt, ids, batch, loss_mask=mask, warmup=2)
+
     def step():
+        if graphed is not None:
+            return graphed.step()
         torch.manual_seed(args.seed + rank)
         return train_fn(ids, model, o, teacher_batch=batch, loss_mask=mask, optimizer=opt)
 
@@ -230,7 +240,7 @@ def main():
         local_ms = start.elapsed_time(end) / args.steps
         clk = clocks.stop()
         ms = max_over_ranks(local_ms, world, dev)
-        loss = result.metrics.loss.item()
+        loss = float(result.metrics.loss)
 
         # End-to-end through the public API: pinned host inputs -> device every step,
         # loss read back every step.
@@ -254,9 +264,12 @@ def main():
                 d_states = [s.to(dev, non_blocking=True) for s in h_states]
                 d_last = h_last.to(dev, non_blocking=True)
                 d_mask = h_mask.to(dev, non_blocking=True)
-                torch.manual_seed(args.seed + rank)
-                r = train_fn(d_ids, model, o, teacher_batch=TB(d_states, d_last), loss_mask=d_mask,
-                             optimizer=opt)
+                if graphed is not None:
+                    r = graphed.step(ids=d_ids, hidden_states=d_states, last_hidden=d_last, loss_mask=d_mask)
+                else:
+                    torch.manual_seed(args.seed + rank)
+                    r = train_fn(d_ids, model, o, teacher_batch=TB(d_states, d_last), loss_mask=d_mask,
+                                 optimizer=opt)
                 losses[i] = r.metrics.loss.float().cpu()
             e1.record()
             torch.cuda.synchronize()
@@ -293,6 +306,7 @@ def main():
                 "global_batch": n, "seq_len": args.seq_len, "anchors": args.anchors,
                 "block_size": 7, "parallelism": f"fsdp{n}" if n > 1 else "single",
                 "comm": (args.comm if args.impl == "ours" else "nccl") if n > 1 else None,
+                "cuda_graph": graphed is not None,
                 "optimizer": "AdamW fp32 masters, lr 1e-5, wd 0.01",
                 "l2": "per-step working set (weights, fp32 masters and moments) far exceeds the 126 MB L2",
             },

@@ -10,6 +10,7 @@ void linear(at::Tensor x, at::Tensor w, at::Tensor out, c10::optional<at::Tensor
 void linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor out, bool accumulate);
 void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate);
 void gemm_test(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int splits);
+void gemm_trace(c10::optional<at::Tensor> buf);
 void rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, at::Tensor y, at::Tensor inv);
 void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor inv, at::Tensor w, at::Tensor dx, at::Tensor dw,
                   c10::optional<at::Tensor> res);
@@ -66,6 +67,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_dgrad", &ns::linear_dgrad);
   m.def("linear_wgrad", &ns::linear_wgrad);
   m.def("gemm_test", &ns::gemm_test);
+  m.def("gemm_trace", &ns::gemm_trace);
   m.def("rms_norm_fwd", &ns::rms_norm_fwd);
   m.def("rms_norm_bwd", &ns::rms_norm_bwd);
   m.def("head_norm_rope_fwd", &ns::head_norm_rope_fwd);

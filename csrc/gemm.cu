@@ -15,10 +15,11 @@
 //   warps 2-5: epilogue, tcgen05.ld of the accumulator (each warp owns the TMEM
 //              lane quarter warp % 4), then bf16/fp32 stores with optional
 //              residual / accumulate.
-// Split-K: every split writes an fp32 partial; the last CTA of a tile to finish
-// (per-tile arrival counter) sums the partials in split order 0..S-1 and runs the
-// epilogue, so results are deterministic and no second kernel is launched.
-// Grids are sized so all CTAs are co-resident (two per SM): one full wave.
+// K depth per stage: 128 for small-N tiles (weight-streaming products, where the
+// per-stage handshake between producer, MMA issuer and barrier dominates), 64 for
+// wide tiles. Split-K: every split writes an fp32 partial; the last CTA of a tile to
+// finish (per-tile arrival counter) sums the partials in split order 0..S-1 and
+// runs the epilogue, so results are deterministic and no second kernel is launched.
 // Every mbarrier wait is bounded; a timeout sets the device error flag.
 #include <map>
 
@@ -29,7 +30,6 @@
 namespace ns {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
 
 struct GemmArgs {
   int M, N, K;
@@ -45,21 +45,24 @@ struct GemmArgs {
   int ws_t;
   unsigned* counters;  // per-tile arrival counters (zero between launches)
   int* err;
+  long long* trace;  // test hook: clock stamps of CTA 0 and per-CTA phase times, or null
 };
 
 template <int BN>
 struct GemmCfg {
+  static constexpr int BK = BN <= 128 ? 128 : 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // Ring depth: two CTAs per SM when the grid has more CTAs than SMs (epilogues
-  // overlap mainloops); otherwise one CTA per SM with the deepest ring that fits,
-  // so weight-streaming products keep ~200 KB of loads in flight per SM.
+  // overlap mainloops); otherwise one CTA per SM with the deepest ring that fits.
   static constexpr int STAGES = (110 * 1024) / STAGE_BYTES;
   static constexpr int STAGES_SOLO = (224 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int SMEM_MAX = STAGES_SOLO * STAGE_BYTES + 1024 + 256;
 };
+
+static int bk_for(int bn) { return bn <= 128 ? 128 : 64; }
 
 __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, float acc) {
   if (a.out_f32) {
@@ -104,6 +107,8 @@ __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      GemmArgs args, int stages) {
   using C = GemmCfg<BN>;
+  constexpr int BK = C::BK;
+  constexpr int KATOMS = BK / 64;  // 128-byte swizzle atoms along K per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -117,6 +122,16 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, split = blockIdx.z;
+  const int cta_id = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  auto stamp = [&](int phase) {
+    if (args.trace && threadIdx.x == 0 && cta_id < 2048) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      args.trace[512 + phase * 2048 + cta_id] = (long long)t;
+    }
+  };
+  const bool trace0 = args.trace && cta_id == 0;
+  stamp(0);
   const int kb_total = (args.K + BK - 1) / BK;
   const int kb0 = split * args.kpb;
   const int kb1 = min(kb0 + args.kpb, kb_total);
@@ -140,6 +155,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  stamp(1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -148,21 +164,24 @@ __global__ void __launch_bounds__(192, 1)
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (i >= stages && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
+        if (trace0 && i < 256) args.trace[i] = clock64();
         sm100::mbar_expect_tx(&full[s], C::STAGE_BYTES);
         const int k = (kb0 + i) * BK;
         uint8_t* a_dst = sA + s * C::A_BYTES;
         uint8_t* b_dst = sB + s * C::B_BYTES;
         if (!AMN) {
-          sm100::tma_load_2d(a_dst, &ta, &full[s], k, m0);
+#pragma unroll
+          for (int j = 0; j < KATOMS; ++j) sm100::tma_load_2d(a_dst + j * (BM * 128), &ta, &full[s], k + 64 * j, m0);
         } else {
           sm100::tma_load_2d(a_dst, &ta, &full[s], m0, k);
-          sm100::tma_load_2d(a_dst + 8192, &ta, &full[s], m0 + 64, k);
+          sm100::tma_load_2d(a_dst + BK * 128, &ta, &full[s], m0 + 64, k);
         }
         if (!BMN) {
-          sm100::tma_load_2d(b_dst, &tb, &full[s], k, n0);
+#pragma unroll
+          for (int j = 0; j < KATOMS; ++j) sm100::tma_load_2d(b_dst + j * (BN * 128), &tb, &full[s], k + 64 * j, n0);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(b_dst + j * 8192, &tb, &full[s], n0 + 64 * j, k);
+          for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(b_dst + j * (BK * 128), &tb, &full[s], n0 + 64 * j, k);
         }
         issued = i + 1;
       }
@@ -177,16 +196,20 @@ __global__ void __launch_bounds__(192, 1)
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (!sm100::mbar_wait(&full[s], ph, args.err)) break;
+        if (trace0 && i < 256) args.trace[256 + i] = clock64();
         sm100::tc_fence_after();
         const uint32_t a_base = sm100::smem_u32(sA + s * C::A_BYTES);
         const uint32_t b_base = sm100::smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          // K-major: 16 bf16 = 32 bytes along the swizzled row; MN-major: 16 rows of 128 B.
-          const uint64_t ad = AMN ? sm100::smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
-                                  : sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
-          const uint64_t bd = BMN ? sm100::smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
-                                  : sm100::smem_desc_sw128(b_base + kk * 32, 0, 1024);
+          // K-major: swizzle atom kk/4 (128 B of K), 32 bytes per 16-element slice inside it.
+          // MN-major: 16 rows of 128 B per slice; the second 64-wide M/N half sits BK*128 B on.
+          const uint64_t ad =
+              AMN ? sm100::smem_desc_sw128(a_base + kk * 2048, BK * 128, 1024)
+                  : sm100::smem_desc_sw128(a_base + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 0, 1024);
+          const uint64_t bd =
+              BMN ? sm100::smem_desc_sw128(b_base + kk * 2048, BK * 128, 1024)
+                  : sm100::smem_desc_sw128(b_base + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 0, 1024);
           sm100::mma_bf16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         sm100::mma_commit(&empty[s]);
@@ -221,8 +244,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
+  stamp(2);
   sm100::tc_fence_before();
   __syncthreads();
+  stamp(3);
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, C::TMEM_COLS);
@@ -240,46 +265,55 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     if (*last_flag) {
       __threadfence();
-      // Groups of 4 consecutive elements along the partials' contiguous dimension;
-      // all split loads of a group are issued before the ordered sum.
-      const int inner = args.ws_t ? BM : BN;   // contiguous extent inside the tile
+      // Groups of 4 consecutive elements along the partials' contiguous dimension.
+      // Each thread keeps U groups in flight: all their loads of one split are
+      // issued before any is consumed (the loop is load-latency bound otherwise).
+      constexpr int U = 4;
+      const int inner = args.ws_t ? BM : BN;
       const int outer = args.ws_t ? BN : BM;
       const int ginner = inner / 4;
+      const int G = ginner * outer;
       const int64_t ld = args.ws_t ? args.M : args.N;
       const bool vec = (ld % 4) == 0;
-      for (int g = threadIdx.x; g < ginner * outer; g += blockDim.x) {
-        const int o = g / ginner, i4 = (g % ginner) * 4;
-        const int gm0 = args.ws_t ? m0 + i4 : m0 + o;
-        const int gn0 = args.ws_t ? n0 + o : n0 + i4;
-        if (gm0 >= args.M || gn0 >= args.N) continue;
-        const int lim = args.ws_t ? args.M - gm0 : args.N - gn0;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (vec && lim >= 4) {
-          float4 part[8];
-          for (int s0 = 0; s0 < args.splits; s0 += 8) {
-            const int ns = min(8, args.splits - s0);
+      for (int g0 = threadIdx.x; g0 < G; g0 += U * blockDim.x) {
+        int gm[U], gn[U], lim[U];
+        float acc[U][4];
 #pragma unroll
-            for (int s = 0; s < 8; ++s)
-              if (s < ns) part[s] = __ldcg(reinterpret_cast<const float4*>(args.ws + ws_index(args, s0 + s, gm0, gn0)));
+        for (int u = 0; u < U; ++u) {
+          const int g = g0 + u * blockDim.x;
+          const int o = g / ginner, i4 = (g % ginner) * 4;
+          gm[u] = args.ws_t ? m0 + i4 : m0 + o;
+          gn[u] = args.ws_t ? n0 + o : n0 + i4;
+          lim[u] = (g >= G || gm[u] >= args.M || gn[u] >= args.N) ? 0 : (args.ws_t ? args.M - gm[u] : args.N - gn[u]);
 #pragma unroll
-            for (int s = 0; s < 8; ++s)
-              if (s < ns) {
-                acc[0] += part[s].x;
-                acc[1] += part[s].y;
-                acc[2] += part[s].z;
-                acc[3] += part[s].w;
-              }
-          }
-        } else {
-          for (int s = 0; s < args.splits; ++s)
-            for (int e = 0; e < 4 && e < lim; ++e)
-              acc[e] += __ldcg(args.ws + ws_index(args, s, args.ws_t ? gm0 + e : gm0, args.ws_t ? gn0 : gn0 + e));
+          for (int e = 0; e < 4; ++e) acc[u][e] = 0.f;
         }
-        for (int e = 0; e < 4 && e < lim; ++e)
-          store_final(args, args.ws_t ? gm0 + e : gm0, args.ws_t ? gn0 : gn0 + e, acc[e]);
+        for (int s = 0; s < args.splits; ++s) {
+          float4 part[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (vec && lim[u] >= 4) part[u] = __ldcg(reinterpret_cast<const float4*>(args.ws + ws_index(args, s, gm[u], gn[u])));
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (vec && lim[u] >= 4) {
+              acc[u][0] += part[u].x;
+              acc[u][1] += part[u].y;
+              acc[u][2] += part[u].z;
+              acc[u][3] += part[u].w;
+            } else {
+              for (int e = 0; e < 4 && e < lim[u]; ++e)
+                acc[u][e] += __ldcg(args.ws + ws_index(args, s, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e));
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          for (int e = 0; e < 4 && e < lim[u]; ++e)
+            store_final(args, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e, acc[u][e]);
       }
     }
   }
+  stamp(4);
 }
 
 template <int BN, bool AMN, bool BMN>
@@ -344,26 +378,28 @@ static unsigned* split_counters(int tiles) {
   return it->second.first;
 }
 
+static long long* g_trace = nullptr;  // test hook (gemm_trace)
+
 // D[M,N] = A * B^T with the epilogue `e`.
 void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e, int force_splits) {
   NS_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
   const int bn = pick_bn(N);
-  CUtensorMap ta = A.mn_major ? make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BK, 64)
+  const int bk = bk_for(bn);
+  CUtensorMap ta = A.mn_major ? make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, bk, 64)
                               : make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BM, 64);
-  CUtensorMap tb = B.mn_major ? make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, BK, 64)
+  CUtensorMap tb = B.mn_major ? make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, bk, 64)
                               : make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, bn, 64);
   const int mt = (M + BM - 1) / BM, nt = (N + bn - 1) / bn;
-  const int kb = (K + BK - 1) / BK;
+  const int kb = (K + bk - 1) / bk;
   const int tiles = mt * nt;
   // Split K only until every SM has one CTA: each extra split adds an fp32 partial
-  // round trip, which for the weight-streaming (small-N) products costs more than
-  // the second CTA per SM gains.
+  // round trip and a share of the last CTA's fix-up.
   const int slots = num_sms();
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
   } else if (tiles < slots) {
-    splits = std::max(1, std::min(slots / tiles, kb / 4));
+    splits = std::max(1, std::min(slots / tiles, kb / 2));
   }
   int kpb = (kb + splits - 1) / splits;
   splits = (kb + kpb - 1) / kpb;
@@ -385,6 +421,7 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   a.res_sn = e.rsn;
   a.accumulate = e.accumulate ? 1 : 0;
   a.err = device_error_flag();
+  a.trace = g_trace;
   a.ws_t = (e.sn != 1) ? 1 : 0;
   at::Tensor ws;
   if (splits > 1) {
@@ -462,6 +499,12 @@ void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate) 
   Operand B{x.data_ptr(), T, K, x.stride(0), true};       // B[n=k, r=t] = x[t, k]
   gemm_launch(A, B, Nout, K, T,
               Epilogue{reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr, ld, 1, nullptr, 0, 0, accumulate});
+}
+
+// Test hook: record clock64 stamps (TMA issue [0,256), MMA start [256,512)) of CTA 0
+// and per-CTA globaltimer phase stamps [512 + phase * 2048 + cta].
+void gemm_trace(c10::optional<at::Tensor> buf) {
+  g_trace = (buf && buf->defined()) ? reinterpret_cast<long long*>(buf->data_ptr<int64_t>()) : nullptr;
 }
 
 // Test hook: plain D = A * B^T with explicit operand majors and a forced split count.

@@ -71,3 +71,37 @@ def test_train_step_deterministic():
     for a, b in zip(out[0][0], out[1][0]):
         assert torch.equal(a, b)
     assert torch.equal(out[0][1], out[1][1])
+
+
+@cuda
+def test_graphed_step_matches_eager():
+    from nanospec_b200.graphs import GraphedStep
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    o = N.Objective(num_anchors=8)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    ids = torch.randint(0, c.vocab_size, (1, 128), device="cuda", generator=g)
+    hs = [torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16() for _ in range(2)]
+    last = torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16()
+    mask = torch.ones(1, 128, device="cuda")
+    torch.manual_seed(0)
+    anchors = N.sample_anchors(ids, mask, o)
+    runs = []
+    for graphed in (False, True):
+        m = _model(c, "cuda", torch.bfloat16)
+        opt = N.AdamW(m.sharding, lr=1e-3)
+        losses = []
+        if graphed:
+            gs = GraphedStep(m, o, opt, ids, N.TeacherBatch(hs, last), loss_mask=mask, anchors=anchors, warmup=1)
+            for _ in range(3):
+                losses.append(float(gs.step().metrics.loss))
+        else:
+            for _ in range(4):  # the graphed run also performs one eager warm-up step
+                r = N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last), loss_mask=mask, anchors=anchors,
+                            optimizer=opt)
+                losses.append(float(r.metrics.loss))
+            losses = losses[1:]
+        runs.append((losses, [s.master.clone() for s in m.sharding], opt.steps))
+    assert runs[0][0] == runs[1][0]
+    assert runs[0][2] == runs[1][2] == 4
+    for a, b in zip(runs[0][1], runs[1][1]):
+        assert torch.equal(a, b)
