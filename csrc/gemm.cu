@@ -21,10 +21,13 @@
 // finish (per-tile arrival counter) sums the partials in split order 0..S-1 and
 // runs the epilogue, so results are deterministic and no second kernel is launched.
 // Every mbarrier wait is bounded; a timeout sets the device error flag.
+#include <cstdio>
 #include <map>
+#include <mutex>
 
 #include "common.h"
 #include "gemm.h"
+#include "gemm_noalloc.h"
 #include "sm100.cuh"
 
 namespace ns {
@@ -522,3 +525,207 @@ void gemm_test(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
 }
 
 }  // namespace ns
+
+// ----------------------------------------------------------------------------- allocation-free entry
+// The C ABI and its contract (limits, zero state, concurrency) are declared in
+// gemm_noalloc.h. Everything below is new code beside the torch path above: the
+// kernel is the same, only its scratch comes from this file-scope array.
+namespace ns {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NSB_GEMM_NOALLOC_SCRATCH_BYTES];
+
+constexpr size_t kNoallocCountersOff = 0;
+constexpr size_t kNoallocStatusOff = 4u * NSB_GEMM_NOALLOC_MAX_TILES;
+constexpr size_t kNoallocPartialsOff = kNoallocStatusOff + 256;
+static_assert(kNoallocPartialsOff % 256 == 0, "partials must stay 256-byte aligned");
+static_assert(kNoallocPartialsOff + 4ull * NSB_GEMM_NOALLOC_PARTIAL_FLOATS <= NSB_GEMM_NOALLOC_SCRATCH_BYTES,
+              "partial area exceeds the scratch array");
+
+constexpr int kNoallocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static unsigned char* g_noalloc_base[kNoallocMaxDevices] = {nullptr};
+static thread_local char g_noalloc_msg[256] = "";
+
+static int noalloc_fail(int code, const char* what, cudaError_t e = cudaSuccess) {
+  if (e != cudaSuccess) std::snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%s: %s", what, cudaGetErrorString(e));
+  else std::snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%s", what);
+  return code;
+}
+
+template <int BN, bool AMN, bool BMN>
+static cudaError_t noalloc_set_attr() {
+  return cudaFuncSetAttribute(gemm_bf16_kernel<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              GemmCfg<BN>::SMEM_MAX);
+}
+
+template <int BN>
+static cudaError_t noalloc_set_attr_bn() {
+  cudaError_t e;
+  if ((e = noalloc_set_attr<BN, false, false>()) != cudaSuccess) return e;
+  if ((e = noalloc_set_attr<BN, true, false>()) != cudaSuccess) return e;
+  if ((e = noalloc_set_attr<BN, false, true>()) != cudaSuccess) return e;
+  return noalloc_set_attr<BN, true, true>();
+}
+
+// Once per device, with that device current: resolve the scratch address and raise
+// the kernels' shared-memory limit.
+static int noalloc_setup_current(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_base[dev]) return 0;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaGetSymbolAddress(scratch)", e);
+  if ((e = noalloc_set_attr_bn<64>()) != cudaSuccess || (e = noalloc_set_attr_bn<128>()) != cudaSuccess ||
+      (e = noalloc_set_attr_bn<192>()) != cudaSuccess || (e = noalloc_set_attr_bn<256>()) != cudaSuccess)
+    return noalloc_fail(3, "cudaFuncSetAttribute", e);
+  g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+  return 0;
+}
+
+template <int BN, bool AMN, bool BMN>
+static cudaError_t noalloc_launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
+                                     int stages, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  // Same shared-memory reservation as the torch path (TMEM co-residency clamp).
+  const int min_smem = (228 * 1024) / (512 / Cfg::TMEM_COLS + 1) - 1024 + 64;
+  const int smem = std::max(stages * Cfg::STAGE_BYTES + 1024 + 256, std::min(min_smem, Cfg::SMEM_MAX));
+  gemm_bf16_kernel<BN, AMN, BMN><<<grid, 192, smem, st>>>(ta, tb, a, stages);
+  return cudaGetLastError();
+}
+
+template <bool AMN, bool BMN>
+static cudaError_t noalloc_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                                  dim3 grid, int stages, cudaStream_t st) {
+  switch (bn) {
+    case 64: return noalloc_launch_bn<64, AMN, BMN>(ta, tb, a, grid, stages, st);
+    case 128: return noalloc_launch_bn<128, AMN, BMN>(ta, tb, a, grid, stages, st);
+    case 192: return noalloc_launch_bn<192, AMN, BMN>(ta, tb, a, grid, stages, st);
+    default: return noalloc_launch_bn<256, AMN, BMN>(ta, tb, a, grid, stages, st);
+  }
+}
+
+static int noalloc_current(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaGetDevice", e);
+  if (dev < 0 || dev >= kNoallocMaxDevices) return noalloc_fail(1, "device ordinal out of range");
+  *dev_out = dev;
+  return 0;
+}
+
+}  // namespace ns
+
+extern "C" int nsb_gemm_noalloc_setup(int device) {
+  using namespace ns;
+  g_noalloc_msg[0] = 0;
+  if (device < 0 || device >= kNoallocMaxDevices) return noalloc_fail(1, "device ordinal out of range");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaGetDevice", e);
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return noalloc_fail(3, "cudaSetDevice", e);
+  const int rc = noalloc_setup_current(device);
+  cudaSetDevice(prev);
+  return rc;
+}
+
+extern "C" int nsb_gemm_bf16_splitk_noalloc(const void* a, int a_mn_major, long long a_rows, long long a_cols,
+                                            long long a_ld, const void* b, int b_mn_major, long long b_rows,
+                                            long long b_cols, long long b_ld, void* out, long long out_ld, int M,
+                                            int N, int K, int splits, void* stream) {
+  using namespace ns;
+  g_noalloc_msg[0] = 0;
+  if (!a || !b || !out) return noalloc_fail(1, "null operand pointer");
+  if (M <= 0 || N <= 0 || K <= 0) return noalloc_fail(1, "M, N and K must be positive");
+  if (splits < 1 || splits > 16) return noalloc_fail(1, "splits must be in [1, 16]");
+  if ((a_mn_major ? a_rows != K || a_cols != M : a_rows != M || a_cols != K) ||
+      (b_mn_major ? b_rows != K || b_cols != N : b_rows != N || b_cols != K))
+    return noalloc_fail(1, "operand shapes do not match M, N, K and their majors");
+  if (out_ld < N || (reinterpret_cast<uintptr_t>(out) % 16) != 0)
+    return noalloc_fail(1, "out must be 16-byte aligned with a row stride >= N");
+  int dev = 0;
+  if (int rc = noalloc_current(&dev)) return rc;
+  if (!g_noalloc_base[dev])
+    if (int rc = noalloc_setup_current(dev)) return rc;
+
+  const int bn = pick_bn(N);
+  const int bk = bk_for(bn);
+  const int mt = (M + BM - 1) / BM, nt = (N + bn - 1) / bn;
+  const int kb = (K + bk - 1) / bk;
+  const int tiles = mt * nt;
+  const int kpb = (kb + splits - 1) / splits;
+  const int eff_splits = (kb + kpb - 1) / kpb;  // same split plan as the torch path
+  if ((unsigned)tiles > NSB_GEMM_NOALLOC_MAX_TILES) {
+    std::snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%d output tiles exceed the maximum of %u", tiles,
+                  NSB_GEMM_NOALLOC_MAX_TILES);
+    return 2;
+  }
+  if (eff_splits > 1 && (unsigned long long)eff_splits * M * N > NSB_GEMM_NOALLOC_PARTIAL_FLOATS) {
+    std::snprintf(g_noalloc_msg, sizeof(g_noalloc_msg),
+                  "split-K partials need %llu floats; the scratch holds at most %u (splits * M * N)",
+                  (unsigned long long)eff_splits * M * N, NSB_GEMM_NOALLOC_PARTIAL_FLOATS);
+    return 2;
+  }
+  CUtensorMap ta, tb;
+  int sms = 0;
+  try {
+    ta = a_mn_major ? make_tmap_bf16(a, a_rows, a_cols, a_ld, bk, 64) : make_tmap_bf16(a, a_rows, a_cols, a_ld, BM, 64);
+    tb = b_mn_major ? make_tmap_bf16(b, b_rows, b_cols, b_ld, bk, 64) : make_tmap_bf16(b, b_rows, b_cols, b_ld, bn, 64);
+    sms = num_sms();
+  } catch (const std::exception& ex) {
+    return noalloc_fail(1, ex.what());
+  }
+  const bool solo = (long long)tiles * eff_splits <= sms;
+  const int stages = std::max(1, std::min(max_stages(bn, solo), kpb));
+
+  unsigned char* base = g_noalloc_base[dev];
+  GemmArgs ga{};
+  ga.M = M;
+  ga.N = N;
+  ga.K = K;
+  ga.kpb = kpb;
+  ga.splits = eff_splits;
+  ga.out = static_cast<__nv_bfloat16*>(out);
+  ga.out_sm = out_ld;
+  ga.out_sn = 1;
+  ga.ws = reinterpret_cast<float*>(base + kNoallocPartialsOff);
+  ga.ws_t = 0;
+  ga.counters = reinterpret_cast<unsigned*>(base + kNoallocCountersOff);
+  ga.err = reinterpret_cast<int*>(base + kNoallocStatusOff);
+  ga.trace = nullptr;
+  const dim3 grid(mt, nt, eff_splits);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (!a_mn_major && !b_mn_major) e = noalloc_launch<false, false>(bn, ta, tb, ga, grid, stages, st);
+  else if (a_mn_major && !b_mn_major) e = noalloc_launch<true, false>(bn, ta, tb, ga, grid, stages, st);
+  else if (!a_mn_major && b_mn_major) e = noalloc_launch<false, true>(bn, ta, tb, ga, grid, stages, st);
+  else e = noalloc_launch<true, true>(bn, ta, tb, ga, grid, stages, st);
+  if (e != cudaSuccess) return noalloc_fail(3, "kernel launch", e);
+  return 0;
+}
+
+extern "C" int nsb_gemm_noalloc_status(int* status) {
+  using namespace ns;
+  g_noalloc_msg[0] = 0;
+  if (!status) return noalloc_fail(1, "null status pointer");
+  int dev = 0;
+  if (int rc = noalloc_current(&dev)) return rc;
+  if (!g_noalloc_base[dev])
+    if (int rc = noalloc_setup_current(dev)) return rc;
+  cudaError_t e = cudaMemcpy(status, g_noalloc_base[dev] + kNoallocStatusOff, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaMemcpy(status)", e);
+  return 0;
+}
+
+extern "C" int nsb_gemm_noalloc_reset(void* stream) {
+  using namespace ns;
+  g_noalloc_msg[0] = 0;
+  int dev = 0;
+  if (int rc = noalloc_current(&dev)) return rc;
+  if (!g_noalloc_base[dev])
+    if (int rc = noalloc_setup_current(dev)) return rc;
+  cudaError_t e = cudaMemsetAsync(g_noalloc_base[dev], 0, kNoallocPartialsOff, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaMemsetAsync(counters)", e);
+  return 0;
+}
+
+extern "C" const char* nsb_gemm_noalloc_error(void) { return ns::g_noalloc_msg; }
