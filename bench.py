@@ -146,7 +146,7 @@ def build(impl, c, world, rank, dev, dtype, seed):
         import nanospec_b200 as N
         state = N.initialize(c, seed, dtype)
         model = N.DSpark(c, state, emb, head, device=dev, dtype=dtype, group=group, world_size=world, rank=rank)
-        opt = N.AdamW(model.sharding, lr=1e-5, weight_decay=0.01)
+        opt = N.AdamW(model.sharding, lr=1e-5, weight_decay=0.01, lazy_zero=True)
         return model, opt, N.train, N.TeacherBatch
     sys.path.insert(0, REF_PATH)
     from nanospec.distributed import TeacherBatch

@@ -1,20 +1,26 @@
 // Draft attention with the anchor layout (no dense mask, no stored probabilities).
 //
-// Query block j of batch row i (block_size queries x G query heads per KV head)
-// sees the context keys [0, anchors[i, j]) and its own block's draft keys; a
-// block with keep == false sees nothing and outputs zeros (lse = -inf).
-// Keys/values are in split layout: row i*S + t for context token t, row
-// b*S + i*Td + u for draft token u; rows may be strided (K and V live in one
-// [rows, 2*Hk*D] projection output).
+// Query block j of batch row i (block_size queries per head) sees the context keys
+// [0, anchors[i, j]) and its own block's draft keys; a block with keep == false sees
+// nothing and outputs zeros (lse = -inf). Keys/values are in split layout: row
+// i*S + t for context token t, row b*S + i*Td + u for draft token u; rows may be
+// strided (K and V live in one [rows, 2*Hk*D] projection output).
+// Reference semantics: the flex-attention mask of nanospec/dspark.py (anchor prefix +
+// own block), evaluated here without a mask tensor.
 //
-// forward : one CTA per (block j, KV head, batch row); the G*bs query rows of
-//           the block share one key stream (GQA), scores and the online softmax
-//           run in fp32, keys are tiled 32 at a time through shared memory.
-// backward: two deterministic kernels instead of atomics.
-//           dq  - same decomposition as the forward (P recomputed from lse);
-//           dkv - one CTA per (32-key tile, KV head, batch row); it walks the
-//                 query blocks that can see the tile and accumulates dK, dV in
-//                 shared memory in a fixed order.
+// The problem is small (a few hundred query rows per head, at most S + block_size
+// keys each), so the kernels are organised for parallelism and few memory round
+// trips rather than tensor-core throughput:
+//   forward : one CTA per (block j, query head, batch row); key tiles of 64 keys
+//             are fetched with 16-byte loads into shared memory; scores (thread per
+//             key), online softmax (warp per row) and P V (thread per column pair)
+//             run in fp32.
+//   backward: dq  - the same decomposition (P recomputed from lse); it also stores
+//                   delta = rowsum(dO * O) for the dkv kernel;
+//             dkv - one CTA per (key tile, KV head, batch row): 16-key context tiles
+//                   and one tile per draft block. It walks the query blocks (and the
+//                   GQA heads) that see the tile and accumulates dK, dV in registers
+//                   in a fixed order: deterministic, no atomics.
 #include "common.h"
 #include "sm100.cuh"
 
@@ -28,347 +34,548 @@ struct AttnArgs {
   const int64_t* anchors;           // [b, nb]
   const bool* keep;                 // [b, nb]
   float* lse;                       // [b, Hq, Td]
+  float* delta;                     // [b, Hq, Td] rowsum(dO * O), written by dq, read by dkv
   bf16 *out, *dq, *dk, *dv;
   int64_t lddk, lddv;
   int b, S, nb, bs, Hq, Hk;
   float scale;
 };
 
-constexpr int KT = 32;  // keys per tile
+constexpr int NT = 128;    // threads of the forward / dq CTAs
+constexpr int KT = 64;     // keys per tile (forward / dq)
+constexpr int RMAX = 32;   // query rows per CTA (block_size)
 
 __device__ __forceinline__ int64_t key_row(const AttnArgs& a, int bi, int kv) {
   // kv in [0, S) context, [S, S+Td) draft
   return kv < a.S ? (int64_t)bi * a.S + kv : (int64_t)a.b * a.S + (int64_t)bi * a.nb * a.bs + (kv - a.S);
 }
 
-// Visible key index ranges of block j: [0, anchor) and [S + j*bs, S + (j+1)*bs).
-__device__ __forceinline__ int n_visible_tiles(int anchor, int bs) {
-  return (anchor + KT - 1) / KT + (bs + KT - 1) / KT;
-}
-
-// Keys of tile `t` of block j: returns base key index and count.
+// Tile t of block j: context tiles cover [0, anchor) in KT steps, then one tile with
+// the block's own bs draft keys.
 __device__ __forceinline__ void tile_keys(int t, int anchor, int S, int j, int bs, int& k0, int& cnt) {
   const int nctx = (anchor + KT - 1) / KT;
   if (t < nctx) {
     k0 = t * KT;
     cnt = min(KT, anchor - k0);
   } else {
-    const int u = t - nctx;
-    k0 = S + j * bs + u * KT;
-    cnt = min(KT, bs - u * KT);
+    k0 = S + j * bs;
+    cnt = bs;
   }
 }
 
-// ---------------------------------------------------------------------------- forward
-constexpr int MAXR = 8;  // query rows per warp (8 warps -> up to 64 rows per CTA)
+__device__ __forceinline__ float2 bf2f(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
 
-template <int D>
-__global__ void __launch_bounds__(256) attn_fwd_kernel(AttnArgs a) {
-  constexpr int E = (D + 31) / 32;  // elements per lane
-  constexpr int DL = D < 32 ? D : 32;  // lanes holding elements
-  extern __shared__ float sm[];
-  const int j = blockIdx.x, hk = blockIdx.y, bi = blockIdx.z;
-  const int G = a.Hq / a.Hk;
-  const int R = G * a.bs;  // query rows of this CTA
-  const int Td = a.nb * a.bs;
-  float* Kt = sm;               // [D][KT]
-  float* Vs = Kt + D * KT;      // [KT][D]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const bool kp = a.keep[bi * a.nb + j];
-  const int anchor = kp ? (int)a.anchors[bi * a.nb + j] : 0;
-  const int ntiles = kp ? n_visible_tiles(anchor, a.bs) : 0;
+// K/V tile staging: `fetch` issues every 16-byte global load of a tile into
+// registers (ROWS keys x D of head hk, rows >= cnt zero), `store` writes them into
+// shared memory rows of KP bf16. Splitting the two lets a CTA fetch tile t + 1 while
+// it computes on tile t. KP = D + 2 (an odd number of 32-bit words) keeps per-key
+// reads free of bank conflicts.
+template <int D, int ROWS, int NTH>
+struct KVRegs {
+  static constexpr int C = D / 8;  // 16-byte chunks per row
+  static constexpr int IT = (ROWS * C + NTH - 1) / NTH;
+  uint4 k[IT], v[IT];
+};
 
-  // Each warp owns rows r = warp, warp + nw, ...; state kept in registers.
-  float acc[MAXR][E];
-  float mx[MAXR], den[MAXR];
-  float qv[MAXR][E];
-  const int my_rows = (R - warp + nw - 1) / nw;
+template <int D, int ROWS, int NTH>
+__device__ __forceinline__ void fetch_kv(const AttnArgs& a, int bi, int hk, int k0, int cnt,
+                                         KVRegs<D, ROWS, NTH>& r, int tid) {
+  using R = KVRegs<D, ROWS, NTH>;
 #pragma unroll
-  for (int rr = 0; rr < MAXR; ++rr) {
-    mx[rr] = -INFINITY;
-    den[rr] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[rr][e] = 0.f;
-    if (rr < my_rows) {
-      const int r = warp + rr * nw;
-      const int g = r / a.bs, u = r % a.bs;
-      const int h = hk * G + g;
-      const int t = bi * Td + j * a.bs + u;
-      const bf16* qp = a.q + ((int64_t)t * a.Hq + h) * D;
-#pragma unroll
-      for (int e = 0; e < E; ++e) qv[rr][e] = lane < DL ? __bfloat162float(qp[lane + 32 * e]) * a.scale : 0.f;
+  for (int i = 0; i < R::IT; ++i) {
+    const int c = tid + i * NTH;
+    const int kk = c / R::C, d8 = (c % R::C) * 8;
+    r.k[i] = r.v[i] = make_uint4(0, 0, 0, 0);
+    if (c < ROWS * R::C && kk < cnt) {
+      const int64_t row = key_row(a, bi, k0 + kk);
+      r.k[i] = *reinterpret_cast<const uint4*>(a.k + row * a.ldk + hk * D + d8);
+      r.v[i] = *reinterpret_cast<const uint4*>(a.v + row * a.ldv + hk * D + d8);
     }
   }
+}
 
+template <int D, int KP, int ROWS, int NTH>
+__device__ __forceinline__ void store_kv(const KVRegs<D, ROWS, NTH>& r, bf16* Ks, bf16* Vs, int tid) {
+  using R = KVRegs<D, ROWS, NTH>;
+#pragma unroll
+  for (int i = 0; i < R::IT; ++i) {
+    const int c = tid + i * NTH;
+    if (c < ROWS * R::C) {
+      const int kk = c / R::C, d8 = (c % R::C) * 8;
+      uint32_t* kd = reinterpret_cast<uint32_t*>(Ks + kk * KP + d8);
+      uint32_t* vd = reinterpret_cast<uint32_t*>(Vs + kk * KP + d8);
+      kd[0] = r.k[i].x;
+      kd[1] = r.k[i].y;
+      kd[2] = r.k[i].z;
+      kd[3] = r.k[i].w;
+      vd[0] = r.v[i].x;
+      vd[1] = r.v[i].y;
+      vd[2] = r.v[i].z;
+      vd[3] = r.v[i].w;
+    }
+  }
+}
+
+// Rows r of block j / head h -> token offset into q/out/dout ([b, Td, Hq, D]).
+__device__ __forceinline__ int64_t qoff(const AttnArgs& a, int bi, int j, int u, int h, int D) {
+  const int Td = a.nb * a.bs;
+  return ((int64_t)(bi * Td + j * a.bs + u) * a.Hq + h) * D;
+}
+
+// ---------------------------------------------------------------------------- forward
+template <int D>
+__global__ void __launch_bounds__(NT) attn_fwd_kernel(AttnArgs a) {
+  constexpr int KP = D + 2;
+  constexpr int NP = D / 2;                       // column pairs
+  constexpr int NG = NT / NP > 0 ? NT / NP : 1;   // row groups in the P V phase
+  constexpr int RPT = (RMAX + NG - 1) / NG;       // rows per thread in the P V phase
+  constexpr int SG = NT / KT;                     // row groups in the score phase
+  constexpr int RS = RMAX / SG;                   // rows per thread in the score phase
+  extern __shared__ __align__(16) uint8_t dyn[];
+  bf16* Ks = reinterpret_cast<bf16*>(dyn);             // [KT][KP]
+  bf16* Vs = Ks + KT * KP;                             // [KT][KP]
+  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RMAX][D] q * scale
+  float* Ps = Qs + RMAX * D;                           // [RMAX][KT]
+  float* mrow = Ps + RMAX * KT;
+  float* lrow = mrow + RMAX;
+  float* corr = lrow + RMAX;
+  const int j = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
+  const int hk = h / (a.Hq / a.Hk);
+  const int R = a.bs, Td = a.nb * a.bs;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool kp = a.keep[bi * a.nb + j];
+  const int anchor = kp ? (int)a.anchors[bi * a.nb + j] : 0;
+  const int ntiles = kp ? (anchor + KT - 1) / KT + 1 : 0;
+
+  for (int c = tid; c < R * (D / 8); c += NT) {
+    const int r = c / (D / 8), d8 = (c % (D / 8)) * 8;
+    const uint4 u = *reinterpret_cast<const uint4*>(a.q + qoff(a, bi, j, r, h, D) + d8);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 f = bf2f(w[t]);
+      Qs[r * D + d8 + 2 * t] = f.x * a.scale;
+      Qs[r * D + d8 + 2 * t + 1] = f.y * a.scale;
+    }
+  }
+  if (tid < RMAX) {
+    mrow[tid] = -INFINITY;
+    lrow[tid] = 0.f;
+  }
+  const int dp = tid % NP, rg = tid / NP;  // P V phase: column pair, row group
+  float acc[RPT][2];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) acc[i][0] = acc[i][1] = 0.f;
+  const int sk = tid % KT, sg = tid / KT;  // score phase: key, row group
+
+  KVRegs<D, KT, NT> kvr;
+  if (ntiles > 0) {
+    int k0, cnt;
+    tile_keys(0, anchor, a.S, j, a.bs, k0, cnt);
+    fetch_kv(a, bi, hk, k0, cnt, kvr, tid);
+  }
   for (int tile = 0; tile < ntiles; ++tile) {
     int k0, cnt;
     tile_keys(tile, anchor, a.S, j, a.bs, k0, cnt);
     __syncthreads();
-    for (int idx = threadIdx.x; idx < KT * D; idx += blockDim.x) {
-      const int kk = idx / D, d = idx % D;
-      float kvv = 0.f, vvv = 0.f;
-      if (kk < cnt) {
-        const int64_t row = key_row(a, bi, k0 + kk);
-        kvv = __bfloat162float(a.k[row * a.ldk + hk * D + d]);
-        vvv = __bfloat162float(a.v[row * a.ldv + hk * D + d]);
+    store_kv<D, KP>(kvr, Ks, Vs, tid);
+    __syncthreads();
+    if (tile + 1 < ntiles) {  // next tile's loads stay in flight during this tile's math
+      int k1, c1;
+      tile_keys(tile + 1, anchor, a.S, j, a.bs, k1, c1);
+      fetch_kv(a, bi, hk, k1, c1, kvr, tid);
+    }
+    // scores s[r][k] = q_r . k_k
+    float s[RS];
+#pragma unroll
+    for (int i = 0; i < RS; ++i) s[i] = 0.f;
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(Ks + sk * KP);
+#pragma unroll 4
+    for (int p = 0; p < NP; ++p) {
+      const float2 kf = bf2f(kr[p]);
+#pragma unroll
+      for (int i = 0; i < RS; ++i) {
+        const int r = sg + SG * i;
+        if (r >= R) break;
+        const float2 qf = *reinterpret_cast<const float2*>(Qs + r * D + 2 * p);
+        s[i] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, s[i]));
       }
-      Kt[d * KT + kk] = kvv;
-      Vs[kk * D + d] = vvv;
+    }
+#pragma unroll
+    for (int i = 0; i < RS; ++i) {
+      const int r = sg + SG * i;
+      if (r < R) Ps[r * KT + sk] = sk < cnt ? s[i] : -INFINITY;
     }
     __syncthreads();
+    // online softmax, one warp per row
+    for (int r = warp; r < R; r += NT / 32) {
+      const float v0 = Ps[r * KT + lane], v1 = Ps[r * KT + lane + 32];
+      float tm = fmaxf(v0, v1);
 #pragma unroll
-    for (int rr = 0; rr < MAXR; ++rr) {
-      if (rr >= my_rows) break;
-      // lane = key: s = q . k_lane
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-#pragma unroll 8
-        for (int dd = 0; dd < DL; ++dd) {
-          const float qd = __shfl_sync(0xffffffff, qv[rr][e], dd);
-          s += qd * Kt[(dd + 32 * e) * KT + lane];
-        }
+      for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffff, tm, o));
+      const float mo = mrow[r];
+      const float mn = fmaxf(mo, tm);
+      float p0 = 0.f, p1 = 0.f, c = 1.f;
+      if (mn > -INFINITY) {
+        p0 = expf(v0 - mn);
+        p1 = expf(v1 - mn);
+        c = mo > -INFINITY ? expf(mo - mn) : 0.f;
       }
-      if (lane >= cnt) s = -INFINITY;
-      float tmax = s;
+      float sum = p0 + p1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffff, tmax, o));
-      const float nm = fmaxf(mx[rr], tmax);
-      const float corr = expf(mx[rr] - nm);
-      const float p = (lane < cnt) ? expf(s - nm) : 0.f;
-      float ps = p;
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+      Ps[r * KT + lane] = p0;
+      Ps[r * KT + lane + 32] = p1;
+      __syncwarp();
+      if (lane == 0) {
+        lrow[r] = lrow[r] * c + sum;
+        mrow[r] = mn;
+        corr[r] = c;
+      }
+    }
+    __syncthreads();
+    // acc[r][d] = acc * corr + sum_k p[r][k] v[k][d]
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffff, ps, o);
-      den[rr] = den[rr] * corr + ps;
-      mx[rr] = nm;
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[rr][e] *= corr;
+    for (int i = 0; i < RPT; ++i) {
+      const int r = rg + NG * i;
+      if (r < R) {
+        acc[i][0] *= corr[r];
+        acc[i][1] *= corr[r];
+      }
+    }
+    if (dp < NP) {
       for (int kk = 0; kk < cnt; ++kk) {
-        const float pk = __shfl_sync(0xffffffff, p, kk);
+        const float2 vf = bf2f(reinterpret_cast<const uint32_t*>(Vs + kk * KP)[dp]);
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[rr][e] += lane < DL ? pk * Vs[kk * D + lane + 32 * e] : 0.f;
+        for (int i = 0; i < RPT; ++i) {
+          const int r = rg + NG * i;
+          if (r >= R) break;
+          const float p = Ps[r * KT + kk];
+          acc[i][0] = fmaf(p, vf.x, acc[i][0]);
+          acc[i][1] = fmaf(p, vf.y, acc[i][1]);
+        }
       }
     }
   }
+  __syncthreads();
 #pragma unroll
-  for (int rr = 0; rr < MAXR; ++rr) {
-    if (rr >= my_rows) break;
-    const int r = warp + rr * nw;
-    const int g = r / a.bs, u = r % a.bs;
-    const int h = hk * G + g;
-    const int t = bi * Td + j * a.bs + u;
-    const bool any = den[rr] > 0.f;
-    const float inv = any ? 1.f / den[rr] : 0.f;
-    bf16* op = a.out + ((int64_t)t * a.Hq + h) * D;
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (lane < DL) op[lane + 32 * e] = __float2bfloat16(acc[rr][e] * inv);
-    if (lane == 0) a.lse[((int64_t)bi * a.Hq + h) * Td + j * a.bs + u] = any ? mx[rr] + logf(den[rr]) : -INFINITY;
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg + NG * i;
+    if (r < R && dp < NP) {
+      const float l = lrow[r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      *reinterpret_cast<__nv_bfloat162*>(a.out + qoff(a, bi, j, r, h, D) + 2 * dp) =
+          __floats2bfloat162_rn(acc[i][0] * inv, acc[i][1] * inv);
+    }
+  }
+  if (tid < R) {
+    const float l = lrow[tid];
+    a.lse[((int64_t)bi * a.Hq + h) * Td + j * a.bs + tid] = l > 0.f ? mrow[tid] + logf(l) : -INFINITY;
   }
 }
 
 // ---------------------------------------------------------------------------- backward dq
 template <int D>
-__global__ void __launch_bounds__(256) attn_bwd_dq_kernel(AttnArgs a) {
-  constexpr int E = (D + 31) / 32;
-  constexpr int DL = D < 32 ? D : 32;
-  extern __shared__ float sm[];
-  const int j = blockIdx.x, hk = blockIdx.y, bi = blockIdx.z;
-  const int G = a.Hq / a.Hk;
-  const int R = G * a.bs;
-  const int Td = a.nb * a.bs;
-  float* Kt = sm;            // [D][KT]
-  float* Ks = Kt + D * KT;   // [KT][D]
-  float* Vt = Ks + KT * D;   // [D][KT]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+__global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(AttnArgs a) {
+  constexpr int KP = D + 2;
+  constexpr int NP = D / 2;
+  constexpr int NG = NT / NP > 0 ? NT / NP : 1;
+  constexpr int RPT = (RMAX + NG - 1) / NG;
+  constexpr int SG = NT / KT;
+  constexpr int RS = RMAX / SG;
+  extern __shared__ __align__(16) uint8_t dyn[];
+  bf16* Ks = reinterpret_cast<bf16*>(dyn);             // [KT][KP]
+  bf16* Vs = Ks + KT * KP;                             // [KT][KP]
+  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RMAX][D] q * scale
+  float* Os = Qs + RMAX * D;                           // [RMAX][D] dO
+  float* Ps = Os + RMAX * D;                           // [RMAX][KT] dS
+  float* lse_s = Ps + RMAX * KT;
+  float* delta_s = lse_s + RMAX;
+  const int j = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
+  const int hk = h / (a.Hq / a.Hk);
+  const int R = a.bs, Td = a.nb * a.bs;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool kp = a.keep[bi * a.nb + j];
   const int anchor = kp ? (int)a.anchors[bi * a.nb + j] : 0;
-  const int ntiles = kp ? n_visible_tiles(anchor, a.bs) : 0;
-  float qv[MAXR][E], dov[MAXR][E], dqa[MAXR][E], lse[MAXR], delta[MAXR];
-  const int my_rows = (R - warp + nw - 1) / nw;
+  const int ntiles = kp ? (anchor + KT - 1) / KT + 1 : 0;
+
+  for (int c = tid; c < R * (D / 8); c += NT) {
+    const int r = c / (D / 8), d8 = (c % (D / 8)) * 8;
+    const int64_t off = qoff(a, bi, j, r, h, D) + d8;
+    const uint4 uq = *reinterpret_cast<const uint4*>(a.q + off);
+    const uint4 uo = *reinterpret_cast<const uint4*>(a.dout + off);
+    const uint32_t wq[4] = {uq.x, uq.y, uq.z, uq.w}, wo[4] = {uo.x, uo.y, uo.z, uo.w};
 #pragma unroll
-  for (int rr = 0; rr < MAXR; ++rr) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) dqa[rr][e] = 0.f;
-    lse[rr] = -INFINITY;
-    delta[rr] = 0.f;
-    if (rr < my_rows) {
-      const int r = warp + rr * nw;
-      const int g = r / a.bs, u = r % a.bs;
-      const int h = hk * G + g;
-      const int t = bi * Td + j * a.bs + u;
-      const int64_t off = ((int64_t)t * a.Hq + h) * D;
-      float dl = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const bool in = lane < DL;
-        qv[rr][e] = in ? __bfloat162float(a.q[off + lane + 32 * e]) * a.scale : 0.f;
-        dov[rr][e] = in ? __bfloat162float(a.dout[off + lane + 32 * e]) : 0.f;
-        dl += in ? dov[rr][e] * __bfloat162float(a.o[off + lane + 32 * e]) : 0.f;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(0xffffffff, dl, o);
-      delta[rr] = dl;
-      lse[rr] = a.lse[((int64_t)bi * a.Hq + h) * Td + j * a.bs + u];
+    for (int t = 0; t < 4; ++t) {
+      const float2 fq = bf2f(wq[t]), fo = bf2f(wo[t]);
+      Qs[r * D + d8 + 2 * t] = fq.x * a.scale;
+      Qs[r * D + d8 + 2 * t + 1] = fq.y * a.scale;
+      Os[r * D + d8 + 2 * t] = fo.x;
+      Os[r * D + d8 + 2 * t + 1] = fo.y;
     }
+  }
+  __syncthreads();
+  for (int r = warp; r < R; r += NT / 32) {
+    const int64_t off = qoff(a, bi, j, r, h, D);
+    float dl = 0.f;
+    for (int d = lane; d < D; d += 32) dl += Os[r * D + d] * __bfloat162float(a.o[off + d]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(0xffffffff, dl, o);
+    if (lane == 0) {
+      const int64_t ri = ((int64_t)bi * a.Hq + h) * Td + j * a.bs + r;
+      delta_s[r] = dl;
+      a.delta[ri] = dl;
+      lse_s[r] = a.lse[ri];
+    }
+  }
+  const int dp = tid % NP, rg = tid / NP;
+  float acc[RPT][2];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) acc[i][0] = acc[i][1] = 0.f;
+  const int sk = tid % KT, sg = tid / KT;
+
+  KVRegs<D, KT, NT> kvr;
+  if (ntiles > 0) {
+    int k0, cnt;
+    tile_keys(0, anchor, a.S, j, a.bs, k0, cnt);
+    fetch_kv(a, bi, hk, k0, cnt, kvr, tid);
   }
   for (int tile = 0; tile < ntiles; ++tile) {
     int k0, cnt;
     tile_keys(tile, anchor, a.S, j, a.bs, k0, cnt);
     __syncthreads();
-    for (int idx = threadIdx.x; idx < KT * D; idx += blockDim.x) {
-      const int kk = idx / D, d = idx % D;
-      float kvv = 0.f, vvv = 0.f;
-      if (kk < cnt) {
-        const int64_t row = key_row(a, bi, k0 + kk);
-        kvv = __bfloat162float(a.k[row * a.ldk + hk * D + d]);
-        vvv = __bfloat162float(a.v[row * a.ldv + hk * D + d]);
+    store_kv<D, KP>(kvr, Ks, Vs, tid);
+    __syncthreads();
+    if (tile + 1 < ntiles) {
+      int k1, c1;
+      tile_keys(tile + 1, anchor, a.S, j, a.bs, k1, c1);
+      fetch_kv(a, bi, hk, k1, c1, kvr, tid);
+    }
+    float s[RS], dpv[RS];
+#pragma unroll
+    for (int i = 0; i < RS; ++i) s[i] = dpv[i] = 0.f;
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(Ks + sk * KP);
+    const uint32_t* vr = reinterpret_cast<const uint32_t*>(Vs + sk * KP);
+#pragma unroll 4
+    for (int p = 0; p < NP; ++p) {
+      const float2 kf = bf2f(kr[p]);
+      const float2 vf = bf2f(vr[p]);
+#pragma unroll
+      for (int i = 0; i < RS; ++i) {
+        const int r = sg + SG * i;
+        if (r >= R) break;
+        const float2 qf = *reinterpret_cast<const float2*>(Qs + r * D + 2 * p);
+        const float2 of = *reinterpret_cast<const float2*>(Os + r * D + 2 * p);
+        s[i] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, s[i]));
+        dpv[i] = fmaf(of.x, vf.x, fmaf(of.y, vf.y, dpv[i]));
       }
-      Kt[d * KT + kk] = kvv;
-      Ks[kk * D + d] = kvv;
-      Vt[d * KT + kk] = vvv;
+    }
+#pragma unroll
+    for (int i = 0; i < RS; ++i) {
+      const int r = sg + SG * i;
+      if (r < R) {
+        const float l = lse_s[r];
+        const float p = (sk < cnt && l > -INFINITY) ? expf(s[i] - l) : 0.f;
+        Ps[r * KT + sk] = p * (dpv[i] - delta_s[r]);
+      }
     }
     __syncthreads();
-#pragma unroll
-    for (int rr = 0; rr < MAXR; ++rr) {
-      if (rr >= my_rows) break;
-      float s = 0.f, dp = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-#pragma unroll 8
-        for (int dd = 0; dd < DL; ++dd) {
-          const float qd = __shfl_sync(0xffffffff, qv[rr][e], dd);
-          const float od = __shfl_sync(0xffffffff, dov[rr][e], dd);
-          s += qd * Kt[(dd + 32 * e) * KT + lane];
-          dp += od * Vt[(dd + 32 * e) * KT + lane];
-        }
-      }
-      const float p = (lane < cnt && lse[rr] > -INFINITY) ? expf(s - lse[rr]) : 0.f;
-      const float ds = p * (dp - delta[rr]);
+    if (dp < NP) {
       for (int kk = 0; kk < cnt; ++kk) {
-        const float dk = __shfl_sync(0xffffffff, ds, kk);
+        const float2 kf = bf2f(reinterpret_cast<const uint32_t*>(Ks + kk * KP)[dp]);
 #pragma unroll
-        for (int e = 0; e < E; ++e) dqa[rr][e] += lane < DL ? dk * Ks[kk * D + lane + 32 * e] : 0.f;
+        for (int i = 0; i < RPT; ++i) {
+          const int r = rg + NG * i;
+          if (r >= R) break;
+          const float ds = Ps[r * KT + kk];
+          acc[i][0] = fmaf(ds, kf.x, acc[i][0]);
+          acc[i][1] = fmaf(ds, kf.y, acc[i][1]);
+        }
       }
     }
   }
 #pragma unroll
-  for (int rr = 0; rr < MAXR; ++rr) {
-    if (rr >= my_rows) break;
-    const int r = warp + rr * nw;
-    const int g = r / a.bs, u = r % a.bs;
-    const int h = hk * G + g;
-    const int t = bi * Td + j * a.bs + u;
-    bf16* dp = a.dq + ((int64_t)t * a.Hq + h) * D;
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (lane < DL) dp[lane + 32 * e] = __float2bfloat16(dqa[rr][e] * a.scale);
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg + NG * i;
+    if (r < R && dp < NP)
+      *reinterpret_cast<__nv_bfloat162*>(a.dq + qoff(a, bi, j, r, h, D) + 2 * dp) =
+          __floats2bfloat162_rn(acc[i][0] * a.scale, acc[i][1] * a.scale);
   }
 }
 
 // ---------------------------------------------------------------------------- backward dk, dv
-// Tiles: ctx tiles [0, ceil(S/KT)) then one tile per draft block (bs <= 32).
-// For each query block j that sees the tile: warps compute P and dS for the block's
-// rows (lane = key) into shared memory; then thread (key = t % 32, dim chunk t / 32)
-// accumulates dK[key] += dS * q and dV[key] += P * dO over the rows in registers.
-template <int D>
-__global__ void __launch_bounds__(128) attn_bwd_dkv_kernel(AttnArgs a) {
-  constexpr int NT = 128;
-  constexpr int DC = D / (NT / 32);  // dims per thread in the accumulation phase
-  constexpr int RMAX = 64;
-  extern __shared__ float sm[];
-  float* Kt = sm;                 // [D][KT]
-  float* Vt = Kt + D * KT;        // [D][KT]
-  float* Qs = Vt + D * KT;        // [RMAX][D]  (q, unscaled)
-  float* Os = Qs + RMAX * D;      // [RMAX][D]  (dO)
-  float* Ps = Os + RMAX * D;      // [RMAX][KT]
-  float* DSs = Ps + RMAX * KT;    // [RMAX][KT]
+// CTA (tile, KV head, batch row) with TK keys: context tiles [0, S) in TK steps
+// (DRAFT == false) or the bs draft keys of block `tile` (DRAFT == true). For every
+// query block that sees the tile, the rows of all G heads of the group are staged
+// in shared memory; a score phase forms P and dS (thread per key), then thread
+// (column pair, key group) accumulates dK, dV over the rows.
+constexpr int NTK = 256;   // threads of the dkv CTAs
+constexpr int GRMAX = 64;  // G * block_size rows per query block
+
+template <int D, int TK, bool DRAFT>
+__global__ void __launch_bounds__(NTK) attn_bwd_dkv_kernel(AttnArgs a) {
+  constexpr int KP = D + 2;
+  constexpr int NP = D / 2;
+  constexpr int KG = NTK / NP > 0 ? NTK / NP : 1;  // key groups in the accumulation phase
+  constexpr int KPT = (TK + KG - 1) / KG;          // keys per thread there
+  constexpr int SG = NTK / TK;                     // row groups in the score phase
+  constexpr int RS = (GRMAX + SG - 1) / SG;        // rows per thread there
+  extern __shared__ __align__(16) uint8_t dyn[];
+  bf16* Ks = reinterpret_cast<bf16*>(dyn);
+  bf16* Vs = Ks + TK * KP;
+  float* Qs = reinterpret_cast<float*>(Vs + TK * KP);  // [GRMAX][D] q (unscaled)
+  float* Os = Qs + GRMAX * D;                          // [GRMAX][D] dO
+  float* Ps = Os + GRMAX * D;                          // [GRMAX][TK]
+  float* DSs = Ps + GRMAX * TK;                        // [GRMAX][TK]
+  float* lse_s = DSs + GRMAX * TK;                     // [GRMAX]
+  float* delta_s = lse_s + GRMAX;                      // [GRMAX]
   const int tile = blockIdx.x, hk = blockIdx.y, bi = blockIdx.z;
   const int G = a.Hq / a.Hk;
   const int Td = a.nb * a.bs;
-  const int nctx = (a.S + KT - 1) / KT;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = NT / 32;
+  const int GR = G * a.bs;
+  const int tid = threadIdx.x;
   int k0, cnt, jlo, jhi;
-  if (tile < nctx) {
-    k0 = tile * KT;
-    cnt = min(KT, a.S - k0);
+  if (!DRAFT) {
+    k0 = tile * TK;
+    cnt = min(TK, a.S - k0);
     jlo = 0;
     jhi = a.nb;
   } else {
-    const int jb = tile - nctx;
-    k0 = a.S + jb * a.bs;
+    k0 = a.S + tile * a.bs;
     cnt = a.bs;
-    jlo = jb;
-    jhi = jb + 1;
+    jlo = tile;
+    jhi = tile + 1;
   }
-  for (int idx = threadIdx.x; idx < KT * D; idx += NT) {
-    const int kk = idx / D, d = idx % D;
-    float kvv = 0.f, vvv = 0.f;
-    if (kk < cnt) {
-      const int64_t row = key_row(a, bi, k0 + kk);
-      kvv = __bfloat162float(a.k[row * a.ldk + hk * D + d]);
-      vvv = __bfloat162float(a.v[row * a.ldv + hk * D + d]);
-    }
-    Kt[d * KT + kk] = kvv;
-    Vt[d * KT + kk] = vvv;
+  {
+    KVRegs<D, TK, NTK> kvr;
+    fetch_kv(a, bi, hk, k0, cnt, kvr, tid);
+    store_kv<D, KP>(kvr, Ks, Vs, tid);
   }
-  const int key = threadIdx.x & 31;
-  const int d0 = (threadIdx.x >> 5) * DC;
-  float dK[DC], dV[DC];
+  const int dp = tid % NP, kg = tid / NP;
+  float dK[KPT][2], dV[KPT][2];
 #pragma unroll
-  for (int i = 0; i < DC; ++i) dK[i] = dV[i] = 0.f;
-  const int R = G * a.bs;
-  for (int j = jlo; j < jhi; ++j) {
-    if (!a.keep[bi * a.nb + j]) continue;
+  for (int i = 0; i < KPT; ++i) dK[i][0] = dK[i][1] = dV[i][0] = dV[i][1] = 0.f;
+  const int sk = tid % TK, sg = tid / TK;
+
+  // Query blocks that see this tile, in increasing order; rows gr = g * bs + u (head
+  // hk*G + g, token u of the block) are fetched one block ahead into registers.
+  auto visible = [&](int j) {
+    return a.keep[bi * a.nb + j] && (DRAFT || (int)a.anchors[bi * a.nb + j] > k0);
+  };
+  auto next_block = [&](int j) {
+    while (j < jhi && !visible(j)) ++j;
+    return j;
+  };
+  constexpr int C = D / 8;
+  constexpr int RIT = (GRMAX * C + NTK - 1) / NTK;
+  uint4 qr[RIT], orr[RIT];
+  float lse_r = 0.f, delta_r = 0.f;
+  auto fetch_rows = [&](int j) {
+#pragma unroll
+    for (int i = 0; i < RIT; ++i) {
+      const int c = tid + i * NTK;
+      if (c < GR * C) {
+        const int gr = c / C, d8 = (c % C) * 8;
+        const int64_t off = qoff(a, bi, j, gr % a.bs, hk * G + gr / a.bs, D) + d8;
+        qr[i] = *reinterpret_cast<const uint4*>(a.q + off);
+        orr[i] = *reinterpret_cast<const uint4*>(a.dout + off);
+      }
+    }
+    if (tid < GR) {
+      const int64_t ri = ((int64_t)bi * a.Hq + hk * G + tid / a.bs) * Td + j * a.bs + tid % a.bs;
+      lse_r = a.lse[ri];
+      delta_r = a.delta[ri];
+    }
+  };
+  int j = next_block(jlo);
+  if (j < jhi) fetch_rows(j);
+  while (j < jhi) {
     const int anchor = (int)a.anchors[bi * a.nb + j];
-    const int vis = tile < nctx ? max(0, min(cnt, anchor - k0)) : cnt;
-    if (vis <= 0) continue;
-    __syncthreads();  // previous block's Ps/DSs/Qs/Os fully consumed
-    for (int idx = threadIdx.x; idx < R * D; idx += NT) {
-      const int r = idx / D, d = idx % D;
-      const int g = r / a.bs, u = r % a.bs;
-      const int t = bi * Td + j * a.bs + u;
-      const int64_t off = ((int64_t)t * a.Hq + hk * G + g) * D + d;
-      Qs[r * D + d] = __bfloat162float(a.q[off]);
-      Os[r * D + d] = __bfloat162float(a.dout[off]);
-    }
-    __syncthreads();
-    for (int r = warp; r < R; r += nw) {
-      const int g = r / a.bs, u = r % a.bs;
-      const int h = hk * G + g;
-      const int t = bi * Td + j * a.bs + u;
-      const int64_t off = ((int64_t)t * a.Hq + h) * D;
-      float dl = 0.f;
-      for (int d = lane; d < D; d += 32) dl += Os[r * D + d] * __bfloat162float(a.o[off + d]);
+    const int vis = DRAFT ? cnt : max(0, min(cnt, anchor - k0));
+    __syncthreads();  // the previous block's rows are consumed
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(0xffffffff, dl, o);
-      const float lse = a.lse[((int64_t)bi * a.Hq + h) * Td + j * a.bs + u];
-      float s = 0.f, dp = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) {
-        s += Qs[r * D + d] * Kt[d * KT + lane];
-        dp += Os[r * D + d] * Vt[d * KT + lane];
+    for (int i = 0; i < RIT; ++i) {
+      const int c = tid + i * NTK;
+      if (c < GR * C) {
+        const int gr = c / C, d8 = (c % C) * 8;
+        const uint32_t qw[4] = {qr[i].x, qr[i].y, qr[i].z, qr[i].w};
+        const uint32_t ow[4] = {orr[i].x, orr[i].y, orr[i].z, orr[i].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          *reinterpret_cast<float2*>(Qs + gr * D + d8 + 2 * t) = bf2f(qw[t]);
+          *reinterpret_cast<float2*>(Os + gr * D + d8 + 2 * t) = bf2f(ow[t]);
+        }
       }
-      const float p = (lane < vis && lse > -INFINITY) ? expf(s * a.scale - lse) : 0.f;
-      Ps[r * KT + lane] = p;
-      DSs[r * KT + lane] = p * (dp - dl) * a.scale;
+    }
+    if (tid < GR) {
+      lse_s[tid] = lse_r;
+      delta_s[tid] = delta_r;
     }
     __syncthreads();
-    for (int r = 0; r < R; ++r) {
-      const float p = Ps[r * KT + key], ds = DSs[r * KT + key];
+    const int jn = next_block(j + 1);
+    if (jn < jhi) fetch_rows(jn);  // in flight during this block's math
+    j = jn;
+    float s[RS], dpv[RS];
 #pragma unroll
-      for (int i = 0; i < DC; ++i) {
-        dV[i] += p * Os[r * D + d0 + i];
-        dK[i] += ds * Qs[r * D + d0 + i];
+    for (int i = 0; i < RS; ++i) s[i] = dpv[i] = 0.f;
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(Ks + sk * KP);
+    const uint32_t* vr = reinterpret_cast<const uint32_t*>(Vs + sk * KP);
+#pragma unroll 4
+    for (int p = 0; p < NP; ++p) {
+      const float2 kf = bf2f(kr[p]);
+      const float2 vf = bf2f(vr[p]);
+#pragma unroll
+      for (int i = 0; i < RS; ++i) {
+        const int r = sg + SG * i;
+        if (r >= GR) break;
+        const float2 qf = *reinterpret_cast<const float2*>(Qs + r * D + 2 * p);
+        const float2 of = *reinterpret_cast<const float2*>(Os + r * D + 2 * p);
+        s[i] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, s[i]));
+        dpv[i] = fmaf(of.x, vf.x, fmaf(of.y, vf.y, dpv[i]));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < RS; ++i) {
+      const int r = sg + SG * i;
+      if (r < GR) {
+        const float l = lse_s[r];
+        const float p = (sk < vis && l > -INFINITY) ? expf(s[i] * a.scale - l) : 0.f;
+        Ps[r * TK + sk] = p;
+        DSs[r * TK + sk] = p * (dpv[i] - delta_s[r]) * a.scale;
+      }
+    }
+    __syncthreads();
+    if (dp < NP) {
+      for (int r = 0; r < GR; ++r) {
+        const float2 of = *reinterpret_cast<const float2*>(Os + r * D + 2 * dp);
+        const float2 qf = *reinterpret_cast<const float2*>(Qs + r * D + 2 * dp);
+#pragma unroll
+        for (int i = 0; i < KPT; ++i) {
+          const int kk = kg + KG * i;
+          if (kk < TK) {
+            const float p = Ps[r * TK + kk], ds = DSs[r * TK + kk];
+            dV[i][0] = fmaf(p, of.x, dV[i][0]);
+            dV[i][1] = fmaf(p, of.y, dV[i][1]);
+            dK[i][0] = fmaf(ds, qf.x, dK[i][0]);
+            dK[i][1] = fmaf(ds, qf.y, dK[i][1]);
+          }
+        }
       }
     }
   }
-  if (key < cnt) {
-    const int64_t row = key_row(a, bi, k0 + key);
+  if (dp < NP) {
 #pragma unroll
-    for (int i = 0; i < DC; ++i) {
-      a.dk[row * a.lddk + hk * D + d0 + i] = __float2bfloat16(dK[i]);
-      a.dv[row * a.lddv + hk * D + d0 + i] = __float2bfloat16(dV[i]);
+    for (int i = 0; i < KPT; ++i) {
+      const int kk = kg + KG * i;
+      if (kk < cnt) {
+        const int64_t row = key_row(a, bi, k0 + kk);
+        *reinterpret_cast<__nv_bfloat162*>(a.dk + row * a.lddk + hk * D + 2 * dp) =
+            __floats2bfloat162_rn(dK[i][0], dK[i][1]);
+        *reinterpret_cast<__nv_bfloat162*>(a.dv + row * a.lddv + hk * D + 2 * dp) =
+            __floats2bfloat162_rn(dV[i][0], dV[i][1]);
+      }
     }
   }
 }
@@ -392,13 +599,16 @@ static AttnArgs make_args(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor a
   a.S = S;
   NS_CHECK(q.size(1) == a.nb * bs, "q rows must be blocks * block_size");
   NS_CHECK(k.size(0) == (int64_t)a.b * (S + a.nb * bs), "k rows must follow the split layout");
-  NS_CHECK(a.Hq % a.Hk == 0 && (a.Hq / a.Hk) * bs <= 64, "GQA group * block_size must be <= 64");
-  NS_CHECK(bs <= KT, "block_size must be <= 32");
+  NS_CHECK(a.Hq % a.Hk == 0 && (a.Hq / a.Hk) * bs <= GRMAX, "GQA group * block_size must be <= 64");
+  NS_CHECK(bs >= 1 && bs <= RMAX, "block_size must be in [1, 32]");
   a.q = reinterpret_cast<const bf16*>(q.data_ptr());
   a.k = reinterpret_cast<const bf16*>(k.data_ptr());
   a.v = reinterpret_cast<const bf16*>(v.data_ptr());
   a.ldk = k.stride(0);
   a.ldv = v.stride(0);
+  NS_CHECK(reinterpret_cast<uintptr_t>(a.k) % 16 == 0 && reinterpret_cast<uintptr_t>(a.v) % 16 == 0 &&
+               a.ldk % 8 == 0 && a.ldv % 8 == 0,
+           "k/v rows must be 16-byte aligned");
   a.anchors = anchors.data_ptr<int64_t>();
   a.keep = keep.data_ptr<bool>();
   a.scale = 1.f / sqrtf((float)q.size(3));
@@ -407,29 +617,38 @@ static AttnArgs make_args(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor a
 
 template <int D>
 static void fwd_d(AttnArgs a) {
-  const int smem = 2 * D * KT * 4;
-  dim3 grid(a.nb, a.Hk, a.b);
-  attn_fwd_kernel<D><<<grid, 256, smem, stream()>>>(a);
+  constexpr int KP = D + 2;
+  const int smem = 2 * KT * KP * 2 + (RMAX * D + RMAX * KT + 3 * RMAX) * 4;
+  NS_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(a.nb, a.Hq, a.b);
+  attn_fwd_kernel<D><<<grid, NT, smem, stream()>>>(a);
+  NS_CUDA(cudaGetLastError());
+}
+
+template <int D, int TK, bool DRAFT>
+static void dkv_launch(const AttnArgs& a, int tiles) {
+  constexpr int KP = D + 2;
+  const int smem = 2 * TK * KP * 2 + (2 * GRMAX * D + 2 * GRMAX * TK + 2 * GRMAX) * 4;
+  auto kern = attn_bwd_dkv_kernel<D, TK, DRAFT>;
+  NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(tiles, a.Hk, a.b);
+  kern<<<grid, NTK, smem, stream()>>>(a);
   NS_CUDA(cudaGetLastError());
 }
 
 template <int D>
 static void bwd_d(AttnArgs a) {
   {
-    const int smem = 3 * D * KT * 4;
-    if (smem > 48 * 1024) NS_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid(a.nb, a.Hk, a.b);
-    attn_bwd_dq_kernel<D><<<grid, 256, smem, stream()>>>(a);
+    constexpr int KP = D + 2;
+    const int smem = 2 * KT * KP * 2 + (2 * RMAX * D + RMAX * KT + 2 * RMAX) * 4;
+    NS_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dim3 grid(a.nb, a.Hq, a.b);
+    attn_bwd_dq_kernel<D><<<grid, NT, smem, stream()>>>(a);
     NS_CUDA(cudaGetLastError());
   }
-  {
-    const int smem = (2 * D * KT + 2 * 64 * D + 2 * 64 * KT) * 4;
-    NS_CUDA(cudaFuncSetAttribute(attn_bwd_dkv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int tiles = (a.S + KT - 1) / KT + a.nb;
-    dim3 grid(tiles, a.Hk, a.b);
-    attn_bwd_dkv_kernel<D><<<grid, 128, smem, stream()>>>(a);
-    NS_CUDA(cudaGetLastError());
-  }
+  constexpr int TKC = 16;
+  if (a.S > 0) dkv_launch<D, TKC, false>(a, (a.S + TKC - 1) / TKC);
+  dkv_launch<D, RMAX, true>(a, a.nb);
 }
 
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
@@ -455,6 +674,8 @@ void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Ten
   a.dout = reinterpret_cast<const bf16*>(dout.data_ptr());
   a.o = reinterpret_cast<const bf16*>(out.data_ptr());
   a.lse = lse.data_ptr<float>();
+  auto delta = at::empty_like(lse);
+  a.delta = delta.data_ptr<float>();
   a.dq = reinterpret_cast<bf16*>(dq.data_ptr());
   a.dk = reinterpret_cast<bf16*>(dk.data_ptr());
   a.dv = reinterpret_cast<bf16*>(dv.data_ptr());

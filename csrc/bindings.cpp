@@ -25,7 +25,7 @@ void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad);
 void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2);
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
-                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev);
+                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev, bool zero_grad);
 void adam_prepare(at::Tensor norm2, at::Tensor step, double b1, double b2, at::Tensor bc);
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
               at::Tensor out, at::Tensor lse);
@@ -80,7 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_update", &ns::adamw_update, py::arg("param"), py::arg("master"), py::arg("m"), py::arg("v"),
         py::arg("grad"), py::arg("factor"), py::arg("norm2"), py::arg("lr"), py::arg("wd"), py::arg("b1"),
         py::arg("b2"), py::arg("eps"), py::arg("bc1"), py::arg("bc2"), py::arg("max_norm"),
-        py::arg("bc_dev") = py::none());
+        py::arg("bc_dev") = py::none(), py::arg("zero_grad") = true);
   m.def("adam_prepare", &ns::adam_prepare);
   m.def("attn_fwd", &ns::attn_fwd);
   m.def("attn_bwd", &ns::attn_bwd);

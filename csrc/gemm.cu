@@ -21,6 +21,7 @@
 // finish (per-tile arrival counter) sums the partials in split order 0..S-1 and
 // runs the epilogue, so results are deterministic and no second kernel is launched.
 // Every mbarrier wait is bounded; a timeout sets the device error flag.
+#include <cmath>
 #include <cstdio>
 #include <map>
 #include <mutex>
@@ -49,7 +50,17 @@ struct GemmArgs {
   unsigned* counters;  // per-tile arrival counters (zero between launches)
   int* err;
   long long* trace;  // test hook: clock stamps of CTA 0 and per-CTA phase times, or null
+  int tma_store;     // persistent kernel: plain bf16 row-major output written by TMA stores
+  int cluster_red;   // split-K: the splits of a tile form a cluster and reduce through DSMEM
 };
+
+constexpr int CLUSTER_MAX = 8;  // portable cluster size: the largest split count reduced in DSMEM
+
+// fp32 partial tile in shared memory for the cluster reduction: [128 rows][BN + 4]
+// ([BN][128 + 4] when the output is transposed), the padding keeps both the
+// per-row writes and the per-column reads free of bank conflicts.
+__host__ __device__ constexpr int partial_ld(int bn, int ws_t) { return ws_t ? 128 + 4 : bn + 4; }
+__host__ __device__ constexpr int partial_bytes(int bn) { return (bn + 4) * (128 + 4) * 4; }
 
 template <int BN>
 struct GemmCfg {
@@ -66,6 +77,26 @@ struct GemmCfg {
 };
 
 static int bk_for(int bn) { return bn <= 128 ? 128 : 64; }
+
+// Two-phase form of store_final for batches: load the residual / old output of
+// every element first (final_load), then write (final_write).
+__device__ __forceinline__ void final_load(const GemmArgs& a, int m, int n, float& add, float& old) {
+  add = a.res ? __bfloat162float(a.res[m * a.res_sm + n * a.res_sn]) : 0.f;
+  old = 0.f;
+  if (a.accumulate)
+    old = a.out_f32 ? a.out_f32[m * a.out_sm + n * a.out_sn] : __bfloat162float(a.out[m * a.out_sm + n * a.out_sn]);
+}
+
+__device__ __forceinline__ void final_write(const GemmArgs& a, int m, int n, float acc, float add, float old) {
+  if (a.out_f32) {
+    a.out_f32[m * a.out_sm + n * a.out_sn] = a.accumulate ? old + acc : acc;
+    return;
+  }
+  float y = sm100::bf16_round(acc);
+  if (a.res) y = sm100::bf16_round(add + y);
+  if (a.accumulate) y = sm100::bf16_round(old + y);
+  a.out[m * a.out_sm + n * a.out_sn] = __float2bfloat16(y);
+}
 
 __device__ __forceinline__ void store_final(const GemmArgs& a, int m, int n, float acc) {
   if (a.out_f32) {
@@ -93,10 +124,33 @@ __device__ __forceinline__ void store_row32(const GemmArgs& a, int m, int nb, co
     }
     return;
   }
+  // General path: every load (residual, accumulated output) is issued before the
+  // first store, so the 32 read-modify-writes do not serialise on memory latency.
+  const int cnt = min(32, a.N - nb);
+  if (a.out_f32) {
+    float* q = a.out_f32 + m * a.out_sm + nb * a.out_sn;
+    float old[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) old[j] = (a.accumulate && j < cnt) ? q[j * a.out_sn] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < cnt) q[j * a.out_sn] = old[j] + v[j];
+    return;
+  }
+  __nv_bfloat16* p = a.out + m * a.out_sm + nb * a.out_sn;
+  float add[32], old[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const int n = nb + j;
-    if (n < a.N) store_final(a, m, n, v[j]);
+    add[j] = (a.res && j < cnt) ? __bfloat162float(a.res[m * a.res_sm + (int64_t)(nb + j) * a.res_sn]) : 0.f;
+    old[j] = (a.accumulate && j < cnt) ? __bfloat162float(p[j * a.out_sn]) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j >= cnt) break;
+    float y = sm100::bf16_round(v[j]);
+    if (a.res) y = sm100::bf16_round(add[j] + y);
+    if (a.accumulate) y = sm100::bf16_round(old[j] + y);
+    p[j * a.out_sn] = __float2bfloat16(y);
   }
 }
 
@@ -117,7 +171,10 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + stages * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * C::B_BYTES);
+  // barriers after the ring, or after the cluster reduction's partial tile if larger
+  const int ring = stages * C::STAGE_BYTES;
+  const int bar_off = (args.cluster_red && partial_bytes(BN) > ring) ? partial_bytes(BN) : ring;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_off);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -231,7 +288,19 @@ __global__ void __launch_bounds__(192, 1)
         sm100::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
         if (m >= args.M) continue;
         const int nb = n0 + c;
-        if (args.splits > 1) {
+        if (args.splits > 1 && args.cluster_red) {
+          // partial tile into this CTA's own shared memory (the ring is idle now)
+          float* pt = reinterpret_cast<float*>(smem);
+          const int row = q * 32 + lane;
+          if (!args.ws_t) {
+            float4* p = reinterpret_cast<float4*>(pt + row * partial_ld(BN, 0) + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pt[(c + j) * partial_ld(BN, 1) + row] = v[j];
+          }
+        } else if (args.splits > 1) {
           if (!args.ws_t && nb + 32 <= args.N && (args.N % 4) == 0) {
             float4* p = reinterpret_cast<float4*>(args.ws + ws_index(args, split, m, nb));
 #pragma unroll
@@ -255,7 +324,60 @@ __global__ void __launch_bounds__(192, 1)
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, C::TMEM_COLS);
   }
-  if (args.splits > 1) {
+  if (args.splits > 1 && args.cluster_red) {
+    // The S split CTAs of this tile are one cluster: after the barrier each reduces
+    // 1/S of the tile by reading every member's partial (in split order 0..S-1)
+    // through distributed shared memory, then writes the output; a second barrier
+    // keeps every member's shared memory alive until all reads are done.
+    sm100::cluster_sync();
+    const int S = args.splits;
+    const uint32_t rank = sm100::cluster_ctarank();
+    const int inner = args.ws_t ? BM : BN;
+    const int ginner = inner / 4;
+    const int G = ginner * (args.ws_t ? BN : BM);
+    const int per = (G + S - 1) / S;
+    const int g_lo = (int)rank * per, g_hi = min(G, g_lo + per);
+    const int pld = partial_ld(BN, args.ws_t);
+    const uint32_t base = sm100::smem_u32(smem);
+    const bool plain = !args.out_f32 && !args.res && !args.accumulate;
+    for (int g = g_lo + threadIdx.x; g < g_hi; g += blockDim.x) {
+      const int o = g / ginner, i4 = (g % ginner) * 4;
+      const uint32_t off = base + (uint32_t)((o * pld + i4) * 4);
+      float4 part[CLUSTER_MAX];
+#pragma unroll
+      for (int s2 = 0; s2 < CLUSTER_MAX; ++s2)
+        if (s2 < S) part[s2] = sm100::dsmem_ld4(sm100::dsmem_map(off, (uint32_t)s2));
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s2 = 0; s2 < CLUSTER_MAX; ++s2)
+        if (s2 < S) {
+          acc[0] += part[s2].x;
+          acc[1] += part[s2].y;
+          acc[2] += part[s2].z;
+          acc[3] += part[s2].w;
+        }
+      const int gm = args.ws_t ? m0 + i4 : m0 + o;
+      const int gn = args.ws_t ? n0 + o : n0 + i4;
+      if (gm >= args.M || gn >= args.N) continue;
+      const int lim = min(4, args.ws_t ? args.M - gm : args.N - gn);
+      if (plain && lim == 4 && ((args.ws_t ? args.out_sm : args.out_sn) == 1) &&
+          ((args.ws_t ? args.out_sn : args.out_sm) % 4 == 0)) {
+        __nv_bfloat162 h[2] = {__floats2bfloat162_rn(acc[0], acc[1]), __floats2bfloat162_rn(acc[2], acc[3])};
+        *reinterpret_cast<uint2*>(args.out + gm * args.out_sm + gn * args.out_sn) = *reinterpret_cast<uint2*>(h);
+        continue;
+      }
+      float add[4], old[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        add[e] = old[e] = 0.f;
+        if (e < lim) final_load(args, args.ws_t ? gm + e : gm, args.ws_t ? gn : gn + e, add[e], old[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < lim) final_write(args, args.ws_t ? gm + e : gm, args.ws_t ? gn : gn + e, acc[e], add[e], old[e]);
+    }
+    sm100::cluster_sync();
+  } else if (args.splits > 1) {
     // Arrival: the last split CTA of this tile reduces all partials in order.
     if (threadIdx.x == 0) {
       __threadfence();
@@ -269,9 +391,10 @@ __global__ void __launch_bounds__(192, 1)
     if (*last_flag) {
       __threadfence();
       // Groups of 4 consecutive elements along the partials' contiguous dimension.
-      // Each thread keeps U groups in flight: all their loads of one split are
-      // issued before any is consumed (the loop is load-latency bound otherwise).
-      constexpr int U = 4;
+      // Each thread keeps U groups x SB splits of loads in flight before consuming
+      // any (the loop is load-latency bound otherwise); partials are still added in
+      // split order 0..S-1.
+      constexpr int U = 4, SB = 6;
       const int inner = args.ws_t ? BM : BN;
       const int outer = args.ws_t ? BN : BM;
       const int ginner = inner / 4;
@@ -280,6 +403,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool vec = (ld % 4) == 0;
       for (int g0 = threadIdx.x; g0 < G; g0 += U * blockDim.x) {
         int gm[U], gn[U], lim[U];
+        bool full[U];
         float acc[U][4];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -288,35 +412,274 @@ __global__ void __launch_bounds__(192, 1)
           gm[u] = args.ws_t ? m0 + i4 : m0 + o;
           gn[u] = args.ws_t ? n0 + o : n0 + i4;
           lim[u] = (g >= G || gm[u] >= args.M || gn[u] >= args.N) ? 0 : (args.ws_t ? args.M - gm[u] : args.N - gn[u]);
+          full[u] = vec && lim[u] >= 4;
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[u][e] = 0.f;
         }
-        for (int s = 0; s < args.splits; ++s) {
-          float4 part[U];
+        for (int s0 = 0; s0 < args.splits; s0 += SB) {
+          float4 part[SB][U];
 #pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (vec && lim[u] >= 4) part[u] = __ldcg(reinterpret_cast<const float4*>(args.ws + ws_index(args, s, gm[u], gn[u])));
+          for (int j = 0; j < SB; ++j)
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            if (vec && lim[u] >= 4) {
-              acc[u][0] += part[u].x;
-              acc[u][1] += part[u].y;
-              acc[u][2] += part[u].z;
-              acc[u][3] += part[u].w;
-            } else {
-              for (int e = 0; e < 4 && e < lim[u]; ++e)
-                acc[u][e] += __ldcg(args.ws + ws_index(args, s, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e));
+            for (int u = 0; u < U; ++u)
+              if (s0 + j < args.splits && full[u])
+                part[j][u] = __ldcg(reinterpret_cast<const float4*>(args.ws + ws_index(args, s0 + j, gm[u], gn[u])));
+#pragma unroll
+          for (int j = 0; j < SB; ++j) {
+            if (s0 + j >= args.splits) break;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              if (full[u]) {
+                acc[u][0] += part[j][u].x;
+                acc[u][1] += part[j][u].y;
+                acc[u][2] += part[j][u].z;
+                acc[u][3] += part[j][u].w;
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < lim[u])
+                    acc[u][e] += __ldcg(args.ws + ws_index(args, s0 + j, args.ws_t ? gm[u] + e : gm[u],
+                                                           args.ws_t ? gn[u] : gn[u] + e));
+              }
             }
           }
         }
+        float add[U][4], old[U][4];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          for (int e = 0; e < 4 && e < lim[u]; ++e)
-            store_final(args, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e, acc[u][e]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            add[u][e] = old[u][e] = 0.f;
+            if (e < lim[u])
+              final_load(args, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e, add[u][e], old[u][e]);
+          }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (e < lim[u])
+              final_write(args, args.ws_t ? gm[u] + e : gm[u], args.ws_t ? gn[u] : gn[u] + e, acc[u][e], add[u][e],
+                          old[u][e]);
       }
     }
   }
   stamp(4);
+}
+
+// Persistent variant for grids with more tiles than SMs (no split-K): one CTA per SM
+// walks tiles u = blockIdx.x, blockIdx.x + gridDim.x, ... The smem ring runs across
+// tile boundaries (the producer loads the next tile's first k-blocks while the
+// current tile finishes) and the accumulator is double-buffered in TMEM (2 x BN
+// columns), so the epilogue of tile i overlaps the main loop of tile i + 1.
+// Epilogue staging for TMA stores: per epilogue warp two 32 x 64 bf16 boxes (128-byte
+// rows, 128B swizzle), so one box is written while the previous one is stored.
+constexpr int EPI_BOX_BYTES = 32 * 128;
+constexpr int EPI_STAGING = 4 * 2 * EPI_BOX_BYTES;
+
+template <int BN>
+struct PersistCfg {
+  static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  static constexpr int STAGES = (227 * 1024 - 1024 - 256 - EPI_STAGING) / GemmCfg<BN>::STAGE_BYTES;
+  static constexpr int SMEM = STAGES * GemmCfg<BN>::STAGE_BYTES + EPI_STAGING + 1024 + 256;
+};
+
+template <int BN, bool AMN, bool BMN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_persistent(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                         const __grid_constant__ CUtensorMap to, GemmArgs args, int mt, int units) {
+  using C = GemmCfg<BN>;
+  using P = PersistCfg<BN>;
+  constexpr int BK = C::BK;
+  constexpr int KATOMS = BK / 64;
+  constexpr int stages = P::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + stages * C::A_BYTES;
+  uint8_t* sE = sB + stages * C::B_BYTES;  // epilogue staging (1024-aligned: stage sizes are)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + EPI_STAGING);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;  // [2] accumulator buffer complete
+  uint64_t* tempty = tfull + 2;      // [2] accumulator buffer drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (args.K + BK - 1) / BK;
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < stages; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+    }
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&ta);
+    sm100::tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, P::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int m0 = (u % mt) * BM, n0 = (u / mt) * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % stages;
+          if (it >= stages && !sm100::mbar_wait(&empty[s], ((it / stages) & 1) ^ 1, args.err)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_expect_tx(&full[s], C::STAGE_BYTES);
+          const int k = kb * BK;
+          uint8_t* a_dst = sA + s * C::A_BYTES;
+          uint8_t* b_dst = sB + s * C::B_BYTES;
+          if (!AMN) {
+#pragma unroll
+            for (int j = 0; j < KATOMS; ++j) sm100::tma_load_2d(a_dst + j * (BM * 128), &ta, &full[s], k + 64 * j, m0);
+          } else {
+            sm100::tma_load_2d(a_dst, &ta, &full[s], m0, k);
+            sm100::tma_load_2d(a_dst + BK * 128, &ta, &full[s], m0 + 64, k);
+          }
+          if (!BMN) {
+#pragma unroll
+            for (int j = 0; j < KATOMS; ++j) sm100::tma_load_2d(b_dst + j * (BN * 128), &tb, &full[s], k + 64 * j, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(b_dst + j * (BK * 128), &tb, &full[s], n0 + 64 * j, k);
+          }
+        }
+      }
+      for (int i = max(0, it - stages); i < it; ++i) sm100::mbar_wait(&full[i % stages], (i / stages) & 1, args.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_bf16(BM, BN, AMN, BMN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (local >= 2 && !sm100::mbar_wait(&tempty[buf], ((local >> 1) - 1) & 1, args.err)) break;
+        sm100::tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % stages;
+          if (!sm100::mbar_wait(&full[s], (it / stages) & 1, args.err)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_u32(sA + s * C::A_BYTES);
+          const uint32_t b_base = sm100::smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad =
+                AMN ? sm100::smem_desc_sw128(a_base + kk * 2048, BK * 128, 1024)
+                    : sm100::smem_desc_sw128(a_base + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 0, 1024);
+            const uint64_t bd =
+                BMN ? sm100::smem_desc_sw128(b_base + kk * 2048, BK * 128, 1024)
+                    : sm100::smem_desc_sw128(b_base + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 0, 1024);
+            sm100::mma_bf16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          sm100::mma_commit(&empty[s]);
+        }
+        if (ok) sm100::mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    uint8_t* stg = sE + q * 2 * EPI_BOX_BYTES;
+    int local = 0, box = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const int m0 = (u % mt) * BM, n0 = (u / mt) * BN;
+      if (!sm100::mbar_wait(&tfull[buf], (local >> 1) & 1, args.err)) break;
+      sm100::tc_fence_after();
+      const int m = m0 + q * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      if (args.tma_store) {
+        // 64 columns per box: row `lane` of the box is this thread's accumulator row;
+        // 16-byte chunk j lands at chunk j ^ (row % 8) (the 128B swizzle of the map).
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64, ++box) {
+          if (n0 + c >= args.N) break;
+          float v0[32], v1[32];
+          sm100::tmem_ld32(trow + (uint32_t)c, v0);
+          sm100::tmem_ld32(trow + (uint32_t)(c + 32), v1);
+          uint8_t* sb = stg + (box & 1) * EPI_BOX_BYTES;
+          if (lane == 0) sm100::bulk_wait_read<1>();  // the store that used `sb` has read it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float* src = j < 4 ? v0 + 8 * j : v1 + 8 * (j - 4);
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(src[2 * t], src[2 * t + 1]);
+            *reinterpret_cast<uint4*>(sb + lane * 128 + ((j ^ (lane & 7)) * 16)) = *reinterpret_cast<uint4*>(h);
+          }
+          sm100::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            sm100::tma_store_2d(&to, sb, n0 + c, m0 + q * 32);
+            sm100::bulk_commit();
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          sm100::tmem_ld32(trow + (uint32_t)c, v);
+          if (m < args.M && n0 + c < args.N) store_row32(args, m, n0 + c, v);
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&tempty[buf]);
+    }
+    if (args.tma_store && lane == 0) sm100::bulk_wait<0>();  // stores complete before exit
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, P::TMEM_COLS);
+  }
+}
+
+template <int BN, bool AMN, bool BMN>
+static void launch_persistent_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                 const GemmArgs& a, int mt, int units) {
+  using P = PersistCfg<BN>;
+  auto kern = gemm_bf16_persistent<BN, AMN, BMN>;
+  static bool attr = false;
+  if (!attr) {
+    NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM));
+    attr = true;
+  }
+  const int grid = std::min(units, num_sms());
+  kern<<<grid, 192, P::SMEM, stream()>>>(ta, tb, to, a, mt, units);
+  NS_CUDA(cudaGetLastError());
+}
+
+template <bool AMN, bool BMN>
+static void launch_persistent(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                              const GemmArgs& a, int mt, int units) {
+  switch (bn) {
+    case 64: launch_persistent_bn<64, AMN, BMN>(ta, tb, to, a, mt, units); break;
+    case 128: launch_persistent_bn<128, AMN, BMN>(ta, tb, to, a, mt, units); break;
+    case 192: launch_persistent_bn<192, AMN, BMN>(ta, tb, to, a, mt, units); break;
+    default: launch_persistent_bn<256, AMN, BMN>(ta, tb, to, a, mt, units); break;
+  }
 }
 
 template <int BN, bool AMN, bool BMN>
@@ -332,7 +695,26 @@ static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   // k = 512 / TMEM_COLS CTAs co-reside (an allocation never has to wait), i.e. k+1
   // CTAs (each also pays 1 KB of reserved shared memory) must not fit in 228 KB.
   const int min_smem = (228 * 1024) / (512 / C::TMEM_COLS + 1) - 1024 + 64;
-  const int smem = std::max(stages * C::STAGE_BYTES + 1024 + 256, std::min(min_smem, C::SMEM_MAX));
+  const int ring = stages * C::STAGE_BYTES;
+  const int used = (a.cluster_red ? std::max(ring, partial_bytes(BN)) : ring) + 1024 + 256;
+  const int smem = std::max(used, std::min(min_smem, C::SMEM_MAX));
+  if (a.cluster_red) {
+    // the split CTAs of one tile form a cluster along z
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = grid.z;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NS_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, a, stages));
+    return;
+  }
   kern<<<grid, 192, smem, stream()>>>(ta, tb, a, stages);
   NS_CUDA(cudaGetLastError());
 }
@@ -383,29 +765,91 @@ static unsigned* split_counters(int tiles) {
 
 static long long* g_trace = nullptr;  // test hook (gemm_trace)
 
+// Launch plan: tile width, split count and kernel. Draft GEMMs are mostly thin
+// (tens to hundreds of token rows against a weight), i.e. bandwidth-bound, so the
+// plan minimises a simple time model:
+//   main loop  = k-blocks per CTA x stage bytes / one CTA's streaming rate,
+//   HBM        = bytes that must cross HBM / HBM bandwidth,
+//   fix-up     = splits x fp32 tile / the last CTA's reduction rate,
+// with one CTA per SM for split-K grids (all CTAs co-resident) and persistent CTAs
+// (tiles > SMs, no split) whose epilogues overlap the next tile's main loop.
+struct GemmPlan {
+  int bn, bk, mt, nt, kb, splits, kpb;
+  bool persistent;
+};
+
+static GemmPlan plan_gemm(int M, int N, int K, int force_splits) {
+  const int sms = num_sms();
+  auto base = [&](int bn) {
+    GemmPlan p{};
+    p.bn = bn;
+    p.bk = bk_for(bn);
+    p.mt = (M + BM - 1) / BM;
+    p.nt = (N + bn - 1) / bn;
+    p.kb = (K + p.bk - 1) / p.bk;
+    return p;
+  };
+  auto finish = [&](GemmPlan p, int splits) {
+    p.kpb = (p.kb + splits - 1) / splits;
+    p.splits = (p.kb + p.kpb - 1) / p.kpb;
+    p.persistent = p.splits == 1 && p.mt * p.nt > sms;
+    return p;
+  };
+  if (force_splits > 0) return finish(base(pick_bn(N)), force_splits);
+  // A split's partial tile is reduced through DSMEM by all S CTAs of the cluster
+  // in parallel: about a microsecond of barriers plus one tile of DSMEM reads.
+  constexpr double HBM_BW = 6.5e12, CTA_BW = 9.0e10, RED_BW = 1.5e11, RED_FIXED = 1.0e-6, FIX_BW = 3.0e10;
+  const double a_bytes = 2.0 * M * K, b_bytes = 2.0 * N * K, o_bytes = 2.0 * M * N;
+  GemmPlan best{};
+  double best_cost = 1e30;
+  for (int bn : {64, 128, 192, 256}) {
+    if (bn > 64 && bn - 64 >= N) break;  // a narrower tile already covers N
+    const GemmPlan p = base(bn);
+    const int tiles = p.mt * p.nt;
+    const double stage = (double)(BM + bn) * p.bk * 2;
+    if (tiles > sms) {
+      const double per_sm = std::ceil((double)tiles / sms);
+      const double t_main = per_sm * p.kb * stage / CTA_BW;
+      const double t_hbm = (a_bytes * p.nt + b_bytes + o_bytes) / HBM_BW;
+      const double cost = std::max(t_main, t_hbm);
+      if (cost < best_cost * 0.98) {
+        best_cost = cost;
+        best = finish(p, 1);
+      }
+      continue;
+    }
+    for (int s = 1; s <= std::min(sms / tiles, p.kb); ++s) {
+      const int kpb = (p.kb + s - 1) / s;
+      if ((p.kb + kpb - 1) / kpb != s) continue;  // same plan as a smaller s
+      const double t_main = kpb * stage / CTA_BW;
+      // up to CLUSTER_MAX splits reduce in DSMEM; beyond, the last CTA of a tile
+      // reads every fp32 partial from global memory
+      const bool dsmem = s <= CLUSTER_MAX;
+      const double t_hbm = (a_bytes + b_bytes + o_bytes + (dsmem ? 0.0 : 8.0 * s * M * N)) / HBM_BW;
+      const double t_fix = s == 1 ? 0.0
+                           : dsmem ? RED_FIXED + (double)BM * bn * 4 / RED_BW
+                                   : s * (double)BM * bn * 4 / FIX_BW;
+      const double cost = std::max(t_main, t_hbm) + t_fix;
+      if (cost < best_cost * 0.98) {
+        best_cost = cost;
+        best = finish(p, s);
+      }
+    }
+  }
+  return best;
+}
+
 // D[M,N] = A * B^T with the epilogue `e`.
 void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e, int force_splits) {
   NS_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
-  const int bn = pick_bn(N);
-  const int bk = bk_for(bn);
+  const GemmPlan plan = plan_gemm(M, N, K, force_splits);
+  const int bn = plan.bn, bk = plan.bk, mt = plan.mt, nt = plan.nt;
+  const int tiles = mt * nt;
+  const int splits = plan.splits, kpb = plan.kpb;
   CUtensorMap ta = A.mn_major ? make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, bk, 64)
                               : make_tmap_bf16(A.ptr, A.rows, A.cols, A.ld, BM, 64);
   CUtensorMap tb = B.mn_major ? make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, bk, 64)
                               : make_tmap_bf16(B.ptr, B.rows, B.cols, B.ld, bn, 64);
-  const int mt = (M + BM - 1) / BM, nt = (N + bn - 1) / bn;
-  const int kb = (K + bk - 1) / bk;
-  const int tiles = mt * nt;
-  // Split K only until every SM has one CTA: each extra split adds an fp32 partial
-  // round trip and a share of the last CTA's fix-up.
-  const int slots = num_sms();
-  int splits = 1;
-  if (force_splits > 0) {
-    splits = force_splits;
-  } else if (tiles < slots) {
-    splits = std::max(1, std::min(slots / tiles, kb / 2));
-  }
-  int kpb = (kb + splits - 1) / splits;
-  splits = (kb + kpb - 1) / kpb;
   const bool solo = (int64_t)tiles * splits <= num_sms();
   const int stages = std::max(1, std::min(max_stages(bn, solo), kpb));
 
@@ -426,11 +870,27 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   a.err = device_error_flag();
   a.trace = g_trace;
   a.ws_t = (e.sn != 1) ? 1 : 0;
+  // split-K reduces in DSMEM within a cluster; a count above the portable cluster
+  // size uses fp32 partials in global memory and a last-CTA fix-up
+  a.cluster_red = (splits > 1 && splits <= CLUSTER_MAX && !g_trace) ? 1 : 0;
   at::Tensor ws;
-  if (splits > 1) {
+  if (splits > 1 && !a.cluster_red) {
     ws = at::empty({(int64_t)splits * M * N}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA));
     a.ws = ws.data_ptr<float>();
     a.counters = split_counters(tiles);
+  }
+  if (plan.persistent && !g_trace) {
+    // More tiles than SMs: persistent CTAs with a cross-tile ring and overlapped epilogues.
+    // A plain row-major bf16 output (16-byte aligned rows) leaves through TMA stores.
+    CUtensorMap to = ta;  // placeholder when unused
+    a.tma_store = (e.out && !e.out_f32 && e.sn == 1 && !e.res && !e.accumulate && e.sm % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(e.out) % 16 == 0) ? 1 : 0;
+    if (a.tma_store) to = make_tmap_bf16(e.out, M, N, e.sm, 32, 64);
+    if (!A.mn_major && !B.mn_major) launch_persistent<false, false>(bn, ta, tb, to, a, mt, tiles);
+    else if (A.mn_major && !B.mn_major) launch_persistent<true, false>(bn, ta, tb, to, a, mt, tiles);
+    else if (!A.mn_major && B.mn_major) launch_persistent<false, true>(bn, ta, tb, to, a, mt, tiles);
+    else launch_persistent<true, true>(bn, ta, tb, to, a, mt, tiles);
+    return;
   }
   dim3 grid(mt, nt, splits);
   if (!A.mn_major && !B.mn_major) launch<false, false>(bn, ta, tb, a, grid, stages);

@@ -1,6 +1,8 @@
 // LM head + Markov head + 0.1 CE + 0.9 KL(target || draft), forward and backward,
-// streamed over the vocabulary in chunks so the [tokens, vocab] logits are never
-// materialised (only one [2T, Vc] chunk lives in a scratch buffer).
+// over the vocabulary in chunks. With few tokens (the draft's T is tens to hundreds
+// of rows) one chunk covers the whole vocabulary: the [2T, V] logits live in HBM
+// (tens of MB), each weight streams once per pass, and pass 2 does not recompute
+// them. Larger T falls back to chunks, where pass 2 recomputes each chunk.
 //
 // pass 1, per chunk c (vocab [v0, v0 + Vc)):
 //   L[0:T]  = bf16(h W_c^T) ; L[0:T] = bf16(L + bf16(E1[prev] W2_c^T))   (draft logits)
@@ -9,7 +11,7 @@
 //            target-weighted logit gap sum_v exp(t - m) (t - l), and the label logit.
 // merge    : lse_draft, lse_target, CE (bf16-rounded like F.cross_entropy on bf16
 //            logits) and KL per token.
-// pass 2, per chunk: recompute L, then the logits gradient (CE at the bf16 boundary,
+// pass 2, per chunk: (several chunks) recompute L, then the logits gradient (CE at the bf16 boundary,
 //            KL in fp32), sum_v min(p, q) partials, and
 //            dh (fp32) += dl W_c, de (fp32) += dl W2_c, dW2_c = dl^T E1[prev].
 // All reductions use fixed-order partial buffers: results are run-to-run identical.
@@ -20,7 +22,6 @@
 namespace ns {
 
 using bf16 = __nv_bfloat16;
-constexpr int VPARTS = 4;  // blocks per row per chunk in the stats / grad kernels
 
 struct Stat {
   float ml, zl, mt, zt, s1;
@@ -42,21 +43,48 @@ __device__ __forceinline__ void merge(Stat& a, const Stat& b) {
   a.s1 = a.s1 * fa + b.s1 * fb;
 }
 
-// grid (T, VPARTS): block (t, p) scans columns [p*Vc/VPARTS, ...) of the chunk.
+// Columns [c0, c1) of a row handled by block p of `parts` (a multiple of 8 wide, so
+// 16-byte vector loads stay aligned when the rows are).
+__device__ __forceinline__ void part_range(int vc, int parts, int p, int& c0, int& c1) {
+  const int per = (((vc + parts - 1) / parts) + 7) & ~7;
+  c0 = min(vc, p * per);
+  c1 = min(vc, c0 + per);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(h[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+
+// grid (T, parts): block (t, p) scans its column range of the chunk. `vec`: rows of L
+// and Tt are 16-byte aligned with strides a multiple of 8 (8 columns per load).
 __global__ void head_stats_kernel(const bf16* __restrict__ L, int64_t ldl, const bf16* __restrict__ Tt,
                                   int64_t ldt, int vc, int v0, const int64_t* __restrict__ labels,
-                                  Stat* __restrict__ part, float* __restrict__ label_logit, int chunk, int T) {
+                                  Stat* __restrict__ part, float* __restrict__ label_logit, int chunk, int T,
+                                  int parts, int vec) {
   const int t = blockIdx.x, p = blockIdx.y;
-  const int per = (vc + VPARTS - 1) / VPARTS;
-  const int c0 = p * per, c1 = min(vc, c0 + per);
+  int c0, c1;
+  part_range(vc, parts, p, c0, c1);
   const bf16* lr = L + (int64_t)t * ldl;
   const bf16* tr = Tt + (int64_t)t * ldt;
   Stat s{-INFINITY, 0.f, -INFINITY, 0.f, 0.f};
-  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+  const int cv = vec ? c0 + ((c1 - c0) & ~7) : c0;
+  for (int c = c0 + threadIdx.x * 8; c < cv; c += blockDim.x * 8) {
+    float l[8], tv[8];
+    unpack8(*reinterpret_cast<const uint4*>(lr + c), l);
+    unpack8(*reinterpret_cast<const uint4*>(tr + c), tv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) merge(s, Stat{l[i], 1.f, tv[i], 1.f, tv[i] - l[i]});
+  }
+  for (int c = cv + threadIdx.x; c < c1; c += blockDim.x) {
     const float l = __bfloat162float(lr[c]);
     const float tv = __bfloat162float(tr[c]);
-    Stat o{l, 1.f, tv, 1.f, tv - l};
-    merge(s, o);
+    merge(s, Stat{l, 1.f, tv, 1.f, tv - l});
   }
   // block reduction in fixed order (warp shuffles, then warp 0)
   __shared__ Stat sh[32];
@@ -75,7 +103,7 @@ __global__ void head_stats_kernel(const bf16* __restrict__ L, int64_t ldl, const
   if (threadIdx.x == 0) {
     Stat a = sh[0];
     for (int i = 1; i < (int)(blockDim.x >> 5); ++i) merge(a, sh[i]);
-    part[((int64_t)chunk * VPARTS + p) * T + t] = a;
+    part[((int64_t)chunk * parts + p) * T + t] = a;
     const int64_t lab = labels[t];
     if (lab >= v0 + c0 && lab < v0 + c1) label_logit[t] = __bfloat162float(lr[lab - v0]);
   }
@@ -98,37 +126,52 @@ __global__ void head_merge_kernel(const Stat* __restrict__ part, int nparts, int
   row[t * 6 + 4] = lse_t;
 }
 
-// Pass-2 elementwise: dl and sum_v min(p, q) partials.
+// Pass-2 elementwise: dl and sum_v min(p, q) partials (grid and `vec` as for the stats).
+struct GradRow {
+  float lse_l, lse_t, ce_s, kl_s;
+  int64_t lab;
+};
+
+__device__ __forceinline__ float grad_elem(const GradRow& g, float l, float tv, int64_t v, float& mn) {
+  const float pd = expf(l - g.lse_l);
+  const float pt = expf(tv - g.lse_t);
+  mn += fminf(pd, pt);
+  // CE part at the compute-dtype boundary: bf16(exp(bf16(log_softmax))) * bf16(scale)
+  const float ls = sm100::bf16_round(l - g.lse_l);
+  float dce = sm100::bf16_round(sm100::bf16_round(expf(ls)) * g.ce_s);
+  if (v == g.lab) dce = sm100::bf16_round(dce - g.ce_s);
+  const float dkl = sm100::bf16_round((pd - pt) * g.kl_s);
+  return dce + dkl;
+}
+
 __global__ void head_grad_kernel(const bf16* __restrict__ L, int64_t ldl, const bf16* __restrict__ Tt,
                                  int64_t ldt, int vc, int v0, const int64_t* __restrict__ labels,
                                  const float* __restrict__ weights, const float* __restrict__ row, float ce_w,
                                  float kl_w, float inv_accum, bf16* __restrict__ dl, int64_t lddl,
-                                 float* __restrict__ minpart, int chunk, int T) {
+                                 float* __restrict__ minpart, int chunk, int T, int parts, int vec) {
   const int t = blockIdx.x, p = blockIdx.y;
-  const int per = (vc + VPARTS - 1) / VPARTS;
-  const int c0 = p * per, c1 = min(vc, c0 + per);
-  const float lse_l = row[t * 6 + 3], lse_t = row[t * 6 + 4];
+  int c0, c1;
+  part_range(vc, parts, p, c0, c1);
   const float scale = weights[t] * inv_accum;
-  const float ce_s = sm100::bf16_round(scale * ce_w);
-  const float kl_s = scale * kl_w;
-  const int64_t lab = labels[t];
+  const GradRow g{row[t * 6 + 3], row[t * 6 + 4], sm100::bf16_round(scale * ce_w), scale * kl_w, labels[t]};
   const bf16* lr = L + (int64_t)t * ldl;
   const bf16* tr = Tt + (int64_t)t * ldt;
   bf16* dr = dl + (int64_t)t * lddl;
   float mn = 0.f;
-  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
-    const float l = __bfloat162float(lr[c]);
-    const float tv = __bfloat162float(tr[c]);
-    const float pd = expf(l - lse_l);
-    const float pt = expf(tv - lse_t);
-    mn += fminf(pd, pt);
-    // CE part at the compute-dtype boundary: bf16(exp(bf16(log_softmax))) * bf16(scale)
-    const float ls = sm100::bf16_round(l - lse_l);
-    float dce = sm100::bf16_round(sm100::bf16_round(expf(ls)) * ce_s);
-    if (v0 + c == lab) dce = sm100::bf16_round(dce - ce_s);
-    const float dkl = sm100::bf16_round((pd - pt) * kl_s);
-    dr[c] = __float2bfloat16(dce + dkl);
+  const int cv = vec ? c0 + ((c1 - c0) & ~7) : c0;
+  for (int c = c0 + threadIdx.x * 8; c < cv; c += blockDim.x * 8) {
+    float l[8], tv[8];
+    unpack8(*reinterpret_cast<const uint4*>(lr + c), l);
+    unpack8(*reinterpret_cast<const uint4*>(tr + c), tv);
+    __nv_bfloat162 o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = __floats2bfloat162_rn(grad_elem(g, l[2 * i], tv[2 * i], (int64_t)v0 + c + 2 * i, mn),
+                                   grad_elem(g, l[2 * i + 1], tv[2 * i + 1], (int64_t)v0 + c + 2 * i + 1, mn));
+    *reinterpret_cast<uint4*>(dr + c) = *reinterpret_cast<const uint4*>(o);
   }
+  for (int c = cv + threadIdx.x; c < c1; c += blockDim.x)
+    dr[c] = __float2bfloat16(grad_elem(g, __bfloat162float(lr[c]), __bfloat162float(tr[c]), (int64_t)v0 + c, mn));
   __shared__ float sh[32];
   for (int off = 16; off > 0; off >>= 1) mn += __shfl_xor_sync(0xffffffff, mn, off);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -137,7 +180,7 @@ __global__ void head_grad_kernel(const bf16* __restrict__ L, int64_t ldl, const 
   if (threadIdx.x == 0) {
     float s = 0.f;
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += sh[i];
-    minpart[((int64_t)chunk * VPARTS + p) * T + t] = s;
+    minpart[((int64_t)chunk * parts + p) * T + t] = s;
   }
 }
 
@@ -172,13 +215,23 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
   NS_CHECK(labels.scalar_type() == at::kLong && labels.numel() == T, "labels [T] int64");
   NS_CHECK(weights.scalar_type() == at::kFloat && weights.numel() == T, "weights [T] fp32");
   auto opt = hcat.options();
+  const int64_t R = hcat.size(0);
+  // chunk <= 0: the whole vocabulary in one chunk when the logits and their gradient
+  // ([R + T, V] bf16) fit in 4 GiB; then pass 2 reuses pass 1's logits instead of
+  // recomputing them, and every GEMM below runs once over the full vocabulary.
+  if (chunk <= 0) {
+    const int64_t budget = int64_t(4) << 30;
+    chunk = (R + T) * V * 2 <= budget ? V : std::max<int64_t>(4096, (budget / ((R + T) * 2)) & ~int64_t(127));
+  }
   const int64_t vc = std::min<int64_t>(chunk, V);
   const int nchunks = (int)((V + vc - 1) / vc);
-  const int64_t R = hcat.size(0);
-  auto Lbuf = at::empty({R, vc}, opt);
-  auto dl = at::empty({T, vc}, opt);
-  auto part = at::empty({(int64_t)nchunks * VPARTS * T * 5}, opt.dtype(at::kFloat));
-  auto minpart = at::empty({(int64_t)nchunks * VPARTS * T}, opt.dtype(at::kFloat));
+  const int64_t ldv = (vc + 7) & ~int64_t(7);  // row stride of the logits / gradient buffers (TMA: 16 B)
+  // blocks per row: about four per SM in total, each at least 2048 columns wide
+  const int parts = (int)std::max<int64_t>(1, std::min<int64_t>((4 * num_sms() + T - 1) / T, vc / 2048));
+  auto Lbuf = at::empty({R, ldv}, opt);
+  auto dl = at::empty({T, ldv}, opt);
+  auto part = at::empty({(int64_t)nchunks * parts * T * 5}, opt.dtype(at::kFloat));
+  auto minpart = at::empty({(int64_t)nchunks * parts * T}, opt.dtype(at::kFloat));
   auto label_logit = at::zeros({T}, opt.dtype(at::kFloat));
   auto row = at::zeros({T, 6}, opt.dtype(at::kFloat));
   auto dh32 = at::zeros({T, H}, opt.dtype(at::kFloat));
@@ -192,11 +245,11 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
     // L[0:R, 0:n] = hcat W_c^T   (swap-AB: vocab rows on M, tokens on N)
     Operand W{lm_head.data_ptr<at::BFloat16>() + v0 * H, n, H, H, false};
     Operand X{hcat.data_ptr(), R, H, H, false};
-    gemm_launch(W, X, (int)n, (int)R, (int)H, Epilogue{Lp, nullptr, 1, vc, nullptr, 0, 0, false});
+    gemm_launch(W, X, (int)n, (int)R, (int)H, Epilogue{Lp, nullptr, 1, ldv, nullptr, 0, 0, false});
     if (markov) {
       Operand W2{w2->data_ptr<at::BFloat16>() + v0 * r, n, r, r, false};
       Operand E{e->data_ptr(), T, r, r, false};
-      gemm_launch(W2, E, (int)n, (int)T, (int)r, Epilogue{Lp, nullptr, 1, vc, nullptr, 0, 0, true});
+      gemm_launch(W2, E, (int)n, (int)T, (int)r, Epilogue{Lp, nullptr, 1, ldv, nullptr, 0, 0, true});
     }
   };
   auto target_ptr = [&](int64_t v0, int64_t& ld) -> const bf16* {
@@ -204,8 +257,12 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
       ld = target_logits->stride(0);
       return reinterpret_cast<const bf16*>(target_logits->data_ptr()) + v0;
     }
-    ld = vc;
-    return Lp + T * vc;
+    ld = ldv;
+    return Lp + T * ldv;
+  };
+  auto vec_ok = [&](const bf16* tp, int64_t ldt) -> int {
+    return (reinterpret_cast<uintptr_t>(Lp) % 16 == 0 && reinterpret_cast<uintptr_t>(tp) % 16 == 0 &&
+            ldt % 8 == 0) ? 1 : 0;
   };
 
   // ---------------- pass 1
@@ -214,11 +271,12 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
     logits_chunk(v0, n);
     int64_t ldt;
     const bf16* tp = target_ptr(v0, ldt);
-    head_stats_kernel<<<dim3(T, VPARTS), 256, 0, stream()>>>(Lp, vc, tp, ldt, (int)n, (int)v0, lab, partp,
-                                                            label_logit.data_ptr<float>(), c, (int)T);
+    head_stats_kernel<<<dim3(T, parts), 256, 0, stream()>>>(Lp, ldv, tp, ldt, (int)n, (int)v0, lab, partp,
+                                                           label_logit.data_ptr<float>(), c, (int)T, parts,
+                                                           vec_ok(tp, ldt));
     NS_CUDA(cudaGetLastError());
   }
-  head_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(partp, nchunks * VPARTS, (int)T,
+  head_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(partp, nchunks * parts, (int)T,
                                                            label_logit.data_ptr<float>(), row.data_ptr<float>());
   NS_CUDA(cudaGetLastError());
 
@@ -226,31 +284,31 @@ std::vector<at::Tensor> head_loss(at::Tensor hcat, int64_t T, at::Tensor lm_head
   auto* dlp = reinterpret_cast<bf16*>(dl.data_ptr());
   for (int c = 0; c < nchunks; ++c) {
     const int64_t v0 = c * vc, n = std::min(vc, V - v0);
-    logits_chunk(v0, n);
+    if (nchunks > 1) logits_chunk(v0, n);  // a single chunk still holds pass 1's logits
     int64_t ldt;
     const bf16* tp = target_ptr(v0, ldt);
-    head_grad_kernel<<<dim3(T, VPARTS), 256, 0, stream()>>>(
-        Lp, vc, tp, ldt, (int)n, (int)v0, lab, weights.data_ptr<float>(), row.data_ptr<float>(), (float)ce_w,
-        (float)kl_w, (float)inv_accum, dlp, vc, minpart.data_ptr<float>(), c, (int)T);
+    head_grad_kernel<<<dim3(T, parts), 256, 0, stream()>>>(
+        Lp, ldv, tp, ldt, (int)n, (int)v0, lab, weights.data_ptr<float>(), row.data_ptr<float>(), (float)ce_w,
+        (float)kl_w, (float)inv_accum, dlp, ldv, minpart.data_ptr<float>(), c, (int)T, parts, vec_ok(tp, ldt));
     NS_CUDA(cudaGetLastError());
     // dh[T, H] += dl[T, n] W_c[n, H]   (swap-AB: H on M, tokens on N, reduce over vocab)
     {
       Operand A{lm_head.data_ptr<at::BFloat16>() + v0 * H, n, H, H, true};
-      Operand B{dlp, T, n, vc, false};
+      Operand B{dlp, T, n, ldv, false};
       gemm_launch(A, B, (int)H, (int)T, (int)n, Epilogue{nullptr, dh32.data_ptr<float>(), 1, H, nullptr, 0, 0, c > 0});
     }
     if (markov) {
       Operand A{w2->data_ptr<at::BFloat16>() + v0 * r, n, r, r, true};
-      Operand B{dlp, T, n, vc, false};
+      Operand B{dlp, T, n, ldv, false};
       gemm_launch(A, B, (int)r, (int)T, (int)n, Epilogue{nullptr, de32.data_ptr<float>(), 1, r, nullptr, 0, 0, c > 0});
       // dW2[v0:v0+n, r] = dl^T E1[prev]
-      Operand DA{dlp, T, n, vc, true};
+      Operand DA{dlp, T, n, ldv, true};
       Operand EB{e->data_ptr(), T, r, r, true};
       gemm_launch(DA, EB, (int)n, (int)r, (int)T,
                   Epilogue{reinterpret_cast<bf16*>(dw2_out->data_ptr()) + v0 * r, nullptr, r, 1, nullptr, 0, 0, false});
     }
   }
-  head_min_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(minpart.data_ptr<float>(), nchunks * VPARTS, (int)T,
+  head_min_merge_kernel<<<(T + 127) / 128, 128, 0, stream()>>>(minpart.data_ptr<float>(), nchunks * parts, (int)T,
                                                                row.data_ptr<float>());
   NS_CUDA(cudaGetLastError());
   auto dh = at::empty({T, H}, opt);

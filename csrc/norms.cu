@@ -351,14 +351,16 @@ __device__ __forceinline__ void adam_one(float g, float& w, float& mm, float& vv
 }
 
 // Fused AdamW over one flat shard: reads grad (bf16), master/m/v (fp32); writes
-// master/m/v, param (bf16) and zeroes grad. 4 elements per thread per iteration
+// master/m/v, param (bf16) and zeroes grad unless `zero_grad` is 0 (the caller
+// guarantees the next backward overwrites every element). 4 elements per thread per iteration
 // (16-byte fp32 and 8-byte bf16 accesses). Skips the update (but still zeroes the
 // gradient) when the global norm in device memory is not finite.
 __global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, float* __restrict__ master,
                                                     float* __restrict__ m, float* __restrict__ v,
                                                     bf16* __restrict__ grad, int64_t n,
                                                     const float* __restrict__ factor,
-                                                    const float* __restrict__ norm2, AdamHyper h) {
+                                                    const float* __restrict__ norm2, AdamHyper h,
+                                                    int zero_grad) {
   const float norm = sqrtf(*norm2);
   const bool finite = isfinite(norm);
   const float clip = finite ? fminf(1.f, h.max_norm / (norm + 1e-6f)) : 0.f;
@@ -410,9 +412,9 @@ __global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, fl
         __stcs(m4 + i, MM[u]);
         __stcs(v4 + i, VV[u]);
         __stcs(p4 + i, *reinterpret_cast<uint2*>(out));
-        __stcs(g4 + i, make_uint2(0u, 0u));
+        if (zero_grad) __stcs(g4 + i, make_uint2(0u, 0u));
       }
-    } else {
+    } else if (zero_grad) {
       g4[i0] = make_uint2(0u, 0u);
       if (has1) g4[i1] = make_uint2(0u, 0u);
     }
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, fl
       v[i] = vv;
       param[i] = __float2bfloat16(w);
     }
-    grad[i] = __float2bfloat16(0.f);
+    if (zero_grad) grad[i] = __float2bfloat16(0.f);
   }
 }
 
@@ -593,7 +595,7 @@ void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2) {
 
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
-                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev) {
+                  double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev, bool zero_grad) {
   const int64_t n = master.numel();
   NS_CHECK(reinterpret_cast<uintptr_t>(master.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(grad.data_ptr()) % 8 == 0 &&
                reinterpret_cast<uintptr_t>(param.data_ptr()) % 8 == 0,
@@ -604,7 +606,7 @@ void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor 
   adamw_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<bf16*>(param.data_ptr()), master.data_ptr<float>(),
                                              m.data_ptr<float>(), v.data_ptr<float>(),
                                              reinterpret_cast<bf16*>(grad.data_ptr()), n, factor.data_ptr<float>(),
-                                             norm2.data_ptr<float>(), h);
+                                             norm2.data_ptr<float>(), h, zero_grad ? 1 : 0);
   NS_CUDA(cudaGetLastError());
 }
 

@@ -125,7 +125,7 @@ def main(argv=None):
     lr = args.learning_rate if args.learning_rate is not None else 1e-5
     if lr <= 0:
         raise ValueError("learning-rate must be positive")
-    opt = AdamW(model.sharding, lr=lr) if model is not None else None
+    opt = AdamW(model.sharding, lr=lr, lazy_zero=True) if model is not None else None
     if model is not None and node.train_gpus > 1 and args.comm == "peer" and node.device.type == "cuda":
         model.sharding.enable_peer(node.train_group)
     start = checkpoint.restore(args.checkpoint, model, opt, o) if (model is not None and args.checkpoint) else 0

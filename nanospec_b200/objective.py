@@ -12,8 +12,9 @@ section of nanospec/train.py:269-311):
 
 ``head_loss`` runs forward AND backward of the whole head: it returns the metrics
 plus ``dh`` (gradient w.r.t. the final-normed hidden), ``de`` (w.r.t. the Markov
-embedding rows) and writes ``dW2``. On CUDA the vocabulary is streamed in chunks
-(``ops/head.py``): the full ``[tokens, vocab]`` logits are never materialised.
+embedding rows) and writes ``dW2``. On CUDA (``ops/head.py``) the logits never
+leave the GPU: with the draft's few tokens the whole ``[2T, vocab]`` block stays in
+HBM for both passes; larger token counts stream the vocabulary in chunks.
 """
 
 from __future__ import annotations

@@ -1,7 +1,8 @@
 """CUDA path of the fused head: LM head + Markov head + CE/KL, vocabulary streamed.
 
-The kernels (csrc/head.cu) never hold more than one ``[2T, chunk]`` slice of the
-logits. They return per-token statistics (CE, KL, sum_v min(p, q), the two log-sum-
+With the draft's few tokens the kernels (csrc/head.cu) hold the whole ``[2T, V]``
+logits in HBM (tens of MB) and stream each weight once per pass; for large T they
+fall back to ``[2T, chunk]`` slices. They return per-token statistics (CE, KL, sum_v min(p, q), the two log-sum-
 exps) and the gradients ``dh``/``de``/``dW2``; the weighted sums and the
 acceptance-length metric are formed here from those per-token values.
 """
@@ -14,7 +15,8 @@ import torch
 
 from ._ext import cuda_ops
 
-VOCAB_CHUNK = int(os.environ.get("NANOSPEC_VOCAB_CHUNK", 16384))
+# 0 = automatic: the whole vocabulary in one chunk while [3T, V] bf16 fits in 4 GiB.
+VOCAB_CHUNK = int(os.environ.get("NANOSPEC_VOCAB_CHUNK", 0))
 
 
 def head_loss_cuda(hidden, lm_head, markov_e, markov_w2, prepared, o, *, target_hidden=None,

@@ -34,15 +34,21 @@ class AdamW:
     On CUDA the step count is kept on the device (it only advances on finite updates,
     which the device decides); ``steps`` reads it back on demand. ``sync=False`` makes
     ``adamw_step`` return 0-dim device tensors instead of Python floats, so a training
-    loop never waits for the GPU between steps.
+    loop never waits for the GPU between steps. ``lazy_zero`` skips writing zeros into
+    single-rank gradients that the next backward overwrites anyway.
     """
 
     def __init__(self, shards, lr=6e-4, weight_decay=0.0, betas=(0.9, 0.999), eps=1e-8,
-                 max_grad_norm=1.0, sync=True):
+                 max_grad_norm=1.0, sync=True, lazy_zero=False):
         self.shards = list(shards)
         self.lr, self.weight_decay, self.betas = lr, weight_decay, tuple(betas)
         self.eps, self.max_grad_norm = eps, max_grad_norm
         self.sync = sync
+        # lazy_zero: on one rank, leave the consumed gradient in place instead of
+        # writing zeros; the shard stays marked ``grad_zero`` and the next backward
+        # binds it directly and overwrites every element (copy semantics), so the
+        # stale values are never read. Saves 2 bytes/parameter of HBM writes.
+        self.lazy_zero = lazy_zero
         self._steps = 0
         self._dev_step = None
 
@@ -111,9 +117,10 @@ def _adamw_cuda(optimizer, den, factor, b1, b2):
     # On the device: advance the step if the norm is finite, form the bias corrections.
     C.adam_prepare(norm2, optimizer._dev_step, float(b1), float(b2), optimizer._bc)
     for s in optimizer.shards:
+        lazy = optimizer.lazy_zero and s.world_size == 1
         C.adamw_update(s.param, s.master, s.m, s.v, s.grad, f, norm2, float(optimizer.lr),
                        float(optimizer.weight_decay), float(b1), float(b2), float(optimizer.eps),
-                       1.0, 1.0, float(optimizer.max_grad_norm), optimizer._bc)
+                       1.0, 1.0, float(optimizer.max_grad_norm), optimizer._bc, not lazy)
         s.grad_zero = True
     norm = norm2.sqrt().reshape(())
     if not optimizer.sync:

@@ -36,7 +36,9 @@ def _seed():
 
 @cuda
 @pytest.mark.parametrize("M,N,K", [(128, 64, 64), (256, 128, 512), (304, 200, 1000), (1024, 256, 4096),
-                                   (128, 192, 128), (5120, 56, 5120), (96, 40, 64)])
+                                   (128, 192, 128), (5120, 56, 5120), (96, 40, 64),
+                                   # more tiles than SMs: persistent kernel (ragged M/N/K edges)
+                                   (2056, 2600, 200), (30720, 56, 384), (4096, 5120, 56)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
 def test_gemm_majors(M, N, K, a_mn, b_mn):
     # TMA needs 16-byte row strides: the contiguous dimension of each operand is a multiple of 8.
@@ -51,7 +53,25 @@ def test_gemm_majors(M, N, K, a_mn, b_mn):
 
 
 @cuda
-@pytest.mark.parametrize("splits", [1, 3, 7])
+def test_linear_family_persistent():
+    # every product has more output tiles than SMs (persistent kernel, residual / accumulate epilogues)
+    T = 4100
+    x = torch.randn(T, 3072, device="cuda").bfloat16()
+    w = (torch.randn(2560, 3072, device="cuda") * 0.05).bfloat16()
+    res = torch.randn(T, 2560, device="cuda").bfloat16()
+    close(ops.linear(x, w, residual=res), res.float() + x.float() @ w.float().t())
+    dy = torch.randn(T, 2560, device="cuda").bfloat16()
+    acc = torch.randn(T, 3072, device="cuda").bfloat16()
+    base = acc.clone()
+    ops.linear_dgrad(dy, w, out=acc, accumulate=True)
+    close(acc, base.float() + dy.float() @ w.float())
+    dw = torch.empty(2560, 3072, device="cuda", dtype=torch.bfloat16)
+    ops.linear_wgrad(dy, x, dw)
+    close(dw, dy.float().t() @ x.float())
+
+
+@cuda
+@pytest.mark.parametrize("splits", [1, 3, 7, 16])  # 3, 7: cluster (DSMEM) reduction; 16: global fix-up
 def test_gemm_splitk_deterministic(splits):
     a = torch.randn(512, 2048, device="cuda").bfloat16()
     b = torch.randn(128, 2048, device="cuda").bfloat16()
@@ -189,12 +209,15 @@ def test_attention(d, hq, hk, S):
 
 
 @cuda
-@pytest.mark.parametrize("markov,teacher_logits", [(True, False), (False, False), (True, True)])
-def test_head_loss(markov, teacher_logits):
+@pytest.mark.parametrize("markov,teacher_logits,chunk", [(True, False, 0), (False, False, 0), (True, True, 0),
+                                                          (True, False, 4096), (True, True, 4096)])
+def test_head_loss(markov, teacher_logits, chunk, monkeypatch):
     import nanospec_b200 as N
+    import nanospec_b200.ops.head as head_mod
     from nanospec_b200.objective import head_loss
+    monkeypatch.setattr(head_mod, "VOCAB_CHUNK", chunk)  # 0: whole vocabulary; 4096: five chunks
     torch.manual_seed(1)
-    V, H, r = 20000, 256, 32
+    V, H, r = 20003, 256, 32  # V % 8 != 0: scalar tails and padded row strides
     b, nb, bs, S = 1, 8, 7, 64
     o = N.Objective(num_anchors=nb, block_size=bs)
     ids = torch.randint(0, V, (b, S))

@@ -105,3 +105,25 @@ def test_graphed_step_matches_eager():
     assert runs[0][2] == runs[1][2] == 4
     for a, b in zip(runs[0][1], runs[1][1]):
         assert torch.equal(a, b)
+
+
+@cuda
+def test_lazy_zero_matches_eager_zero():
+    # Skipping the gradient zeroing on one rank must not change any step's result.
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    o = N.Objective(num_anchors=8)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(0, c.vocab_size, (1, 128), device="cuda", generator=g)
+    hs = [torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16() for _ in range(2)]
+    last = torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16()
+    runs = []
+    for lazy in (False, True):
+        m = _model(c, "cuda", torch.bfloat16)
+        opt = N.AdamW(m.sharding, lr=1e-3, lazy_zero=lazy)
+        torch.manual_seed(11)
+        losses = [float(N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last), optimizer=opt).metrics.loss)
+                  for _ in range(3)]
+        runs.append((losses, [s.master.clone() for s in m.sharding]))
+    assert runs[0][0] == runs[1][0]
+    for a, b in zip(runs[0][1], runs[1][1]):
+        assert torch.equal(a, b)
