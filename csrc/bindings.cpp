@@ -51,6 +51,8 @@ at::Tensor window_ipc_handle(int64_t id);
 void window_open(int64_t id, at::Tensor handles);
 void window_close(int64_t id);
 at::Tensor window_view(int64_t id, int64_t offset, int64_t numel, at::ScalarType dtype);
+void peer_reduce_avg_ce(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad, at::Tensor staging);
+void peer_allgather_ce(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out);
 void peer_allgather(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out);
 void peer_reduce_avg(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad);
 void peer_signal(int64_t id, int64_t flags_off, int64_t channel, int64_t seq);
@@ -99,6 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("window_open", &ns::window_open);
   m.def("window_close", &ns::window_close);
   m.def("window_view", &ns::window_view);
+  m.def("peer_reduce_avg_ce", &ns::peer_reduce_avg_ce);
+  m.def("peer_allgather_ce", &ns::peer_allgather_ce);
   m.def("peer_allgather", &ns::peer_allgather);
   m.def("peer_reduce_avg", &ns::peer_reduce_avg);
   m.def("peer_signal", &ns::peer_signal);

@@ -7,7 +7,8 @@
 //
 // Kernels (all waits are bounded: on timeout they set the device error word and
 // return; nothing traps or spins forever):
-//   peer_allgather   : out[p*ss + i] = window_p[src_off + i]       (pull from every rank)
+//   peer_allgather   : out[p*ss + i] = window_p[src_off + i]       (pull from every rank;
+//                      SM kernel, or copy-engine DMA per shard: peer_allgather_ce)
 //   peer_reduce_avg  : grad[i] += bf16( (sum_p window_p[slot + r*ss + i]) / N )
 //                      summed in fixed rank order (deterministic)
 //   peer_signal/wait : sequence-number flags (release stores to every peer's flag
@@ -78,21 +79,78 @@ __global__ void peer_allgather_kernel(PeerTable t, int world, int64_t src_off, i
 }
 
 // grad[i] = bf16(grad[i] + bf16(sum_p slot_p[rank*ss + i] / world)), fixed p order.
-__global__ void peer_reduce_avg_kernel(PeerTable t, int world, int rank, int64_t slot_off, int64_t ss,
-                                       __nv_bfloat16* grad) {
+// Each thread keeps U chunks x every peer's 16-byte load in flight before summing
+// (remote loads are latency-bound).
+constexpr int RED_U = 2;
+__global__ void __launch_bounds__(256) peer_reduce_avg_kernel(PeerTable t, int world, int rank, int64_t slot_off,
+                                                              int64_t ss, __nv_bfloat16* grad) {
+  const int64_t n8 = ss / 8;
+  const float inv = 1.f / world;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n8; i0 += RED_U * stride) {
+    uint4 v[RED_U][MAX_PEERS];
+    uint4 g[RED_U];
+#pragma unroll
+    for (int u = 0; u < RED_U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n8) {
+#pragma unroll
+        for (int p = 0; p < MAX_PEERS; ++p)
+          if (p < world)
+            v[u][p] = *reinterpret_cast<const uint4*>(t.base[p] + slot_off + ((int64_t)rank * ss + i * 8) * 2);
+        g[u] = reinterpret_cast<const uint4*>(grad)[i];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RED_U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n8) break;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int p = 0; p < MAX_PEERS; ++p) {
+        if (p >= world) break;
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[u][p]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(h[j]);
+      }
+      __nv_bfloat16* gh = reinterpret_cast<__nv_bfloat16*>(&g[u]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        gh[j] = __float2bfloat16(__bfloat162float(gh[j]) + sm100::bf16_round(acc[j] * inv));
+      reinterpret_cast<uint4*>(grad)[i] = g[u];
+    }
+  }
+}
+
+// Second half of the copy-engine reduce: the peers' contributions to this rank's
+// shard were copied by DMA into `staging` ([world][ss], row `rank` unused); sum
+// them with this rank's own slot range in fixed rank order (the same order and
+// rounding as peer_reduce_avg_kernel), 8 elements per thread.
+__global__ void __launch_bounds__(256) local_reduce_avg_kernel(const __nv_bfloat16* __restrict__ own,
+                                                               const __nv_bfloat16* __restrict__ staging,
+                                                               int world, int rank, int64_t ss,
+                                                               __nv_bfloat16* __restrict__ grad) {
   const int64_t n8 = ss / 8;
   const float inv = 1.f / world;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 v[MAX_PEERS];
+#pragma unroll
+    for (int p = 0; p < MAX_PEERS; ++p)
+      if (p < world)
+        v[p] = __ldcs(reinterpret_cast<const uint4*>((p == rank ? own : staging + (int64_t)p * ss)) + i);
+    uint4 g = reinterpret_cast<const uint4*>(grad)[i];
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int p = 0; p < world; ++p) {
-      const uint4 v = *reinterpret_cast<const uint4*>(t.base[p] + slot_off + ((int64_t)rank * ss + i * 8) * 2);
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int p = 0; p < MAX_PEERS; ++p) {
+      if (p >= world) break;
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[p]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(h[j]);
     }
-    uint4 g = reinterpret_cast<uint4*>(grad)[i];
     __nv_bfloat16* gh = reinterpret_cast<__nv_bfloat16*>(&g);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -201,6 +259,18 @@ static int blocks_for(int64_t items) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 4));
 }
 
+// All-gather on the copy engines: one peer-to-peer cudaMemcpyAsync per rank's shard
+// (NVLink DMA, no SMs taken from the overlapped compute).
+void peer_allgather_ce(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out) {
+  Window* w = g_windows.at(id);
+  const int64_t ss_bytes = ss_elems * 2;
+  NS_CHECK(out.numel() * out.element_size() >= ss_bytes * w->world, "all-gather output too small");
+  uint8_t* dst = static_cast<uint8_t*>(out.data_ptr());
+  for (int p = 0; p < w->world; ++p)
+    NS_CUDA(cudaMemcpyAsync(dst + p * ss_bytes, reinterpret_cast<const void*>(w->table.base[p] + src_off), ss_bytes,
+                            cudaMemcpyDeviceToDevice, stream()));
+}
+
 void peer_allgather(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out) {
   Window* w = g_windows.at(id);
   const int64_t ss_bytes = ss_elems * 2;
@@ -228,6 +298,33 @@ void peer_reduce_avg(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor 
   }
   peer_reduce_avg_kernel<<<blocks_for(ss_elems / 8), 256, 0, stream()>>>(
       w->table, w->world, w->rank, slot_off, ss_elems, reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
+  NS_CUDA(cudaGetLastError());
+}
+
+// Reduce on the copy engines: DMA every peer's range [rank*ss, (rank+1)*ss) of its
+// gradient slot into `staging` ([world][ss] bf16), then one local kernel sums the
+// contributions in rank order into `grad`. NVLink traffic takes no SMs.
+void peer_reduce_avg_ce(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad, at::Tensor staging) {
+  Window* w = g_windows.at(id);
+  NS_CHECK(slot_off % 16 == 0, "peer reduce needs a 16-byte aligned slot");
+  NS_CHECK(staging.numel() >= ss_elems * w->world, "reduce staging buffer too small");
+  const int64_t bytes = ss_elems * 2;
+  auto* st = static_cast<uint8_t*>(staging.data_ptr());
+  for (int p = 0; p < w->world; ++p) {
+    if (p == w->rank) continue;
+    NS_CUDA(cudaMemcpyAsync(st + p * bytes, reinterpret_cast<const void*>(w->table.base[p] + slot_off + w->rank * bytes),
+                            bytes, cudaMemcpyDeviceToDevice, stream()));
+  }
+  const auto* own = reinterpret_cast<const __nv_bfloat16*>(w->table.base[w->rank] + slot_off + w->rank * bytes);
+  if (ss_elems % 8 != 0 || reinterpret_cast<uintptr_t>(grad.data_ptr()) % 16 != 0 || (w->rank * bytes) % 16 != 0) {
+    // unaligned shards: the SM pull kernel reads the same values
+    peer_reduce_avg(id, slot_off, ss_elems, grad);
+    return;
+  }
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((ss_elems / 8 + 255) / 256, (int64_t)num_sms() * 2));
+  local_reduce_avg_kernel<<<blocks, 256, 0, stream()>>>(own, reinterpret_cast<const __nv_bfloat16*>(st), w->world,
+                                                        w->rank, ss_elems,
+                                                        reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
   NS_CUDA(cudaGetLastError());
 }
 

@@ -120,6 +120,7 @@ def restore(path, model, optimizer, objective) -> int:
     for k, v in meta["optimizer"].items():
         setattr(optimizer, k, tuple(v) if k == "betas" else v)
     optimizer.steps = state["optimizer_steps"]
+    model.sharding.parameters_changed()
     _set_rng_state(state["rng"], first.param.device)
     return state["step"]
 

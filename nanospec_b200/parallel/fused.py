@@ -4,20 +4,27 @@ Every training rank owns one *window* (a device allocation opened by all peers
 through CUDA IPC). The window holds this rank's parameter shard of every unit, two
 full-size gradient slots and a flag area; peers address it at the same offsets.
 
-* all-gather of unit i: a kernel on the communication stream pulls every rank's
-  shard straight out of the peers' windows over NVLink into a persistent local
-  buffer, one visit ahead of compute (the gathered weights stay resident for the
-  backward pass, so the model is gathered once per step);
+* all-gather: as soon as every rank's parameters are final, the communication
+  stream pulls every unit (in forward order) out of the peers' windows over NVLink
+  into persistent local buffers, by copy-engine DMA (one peer-to-peer copy per
+  shard, no SMs taken from compute) or by an SM kernel; compute waits per unit on
+  an event. The gathered weights stay resident for the backward pass, so the model
+  is gathered once per step;
 * reduce-scatter of unit i: after the backward of unit i writes its full gradient
   into a window slot, each rank signals its peers, and every owner pulls its
-  shard-range of every peer's slot, sums the N contributions in fixed rank order,
-  averages and adds into its gradient shard (deterministic, NCCL AVG semantics);
+  shard-range of every peer's slot (copy-engine DMA into a staging buffer, or an SM
+  kernel), sums the N contributions in fixed rank order, averages and adds into its
+  gradient shard (deterministic, NCCL AVG semantics);
 * synchronisation is by sequence-number flags in the windows (release stores /
   acquire loads) with bounded waits: a peer that never signals makes the wait
   kernel set the device error word and return, and the host raises.
 
 The protocol per step, all ranks in the same order:
-``begin``: barrier "parameters of step t final" (after the previous AdamW);
+``publish`` (from the optimizer, after each shard's update): flag "unit i final"
+and gather unit i for the next step on the communication stream, overlapping the
+rest of the optimizer step;
+``begin``: barrier "parameters of step t final" (after the previous AdamW), then
+gather every unit not gathered by ``publish``;
 ``prefetch/acquire``: gather + event; ``gradient_buffer``: wait until every peer
 has pulled this slot's previous contents; ``reduce``: signal "slot ready", wait for
 all peers' "slot ready", pull-reduce, signal "slot pulled"; ``finish``: the
@@ -36,6 +43,7 @@ from .shard import ScheduleError
 
 FLAGS_BYTES = 4096
 CH_PARAMS, CH_PULLED, CH_READY = 0, 2, 4  # channels; PULLED/READY use +slot
+CH_UNIT = 8  # CH_UNIT + i: "unit i's parameters are final" (published per unit after AdamW)
 
 
 def _align(n, a=256):
@@ -102,6 +110,22 @@ class PeerSchedule:
         self.slot_owner = [None, None]
         t = timeout_s if timeout_s is not None else float(os.environ.get("NANOSPEC_PEER_TIMEOUT_S", 60))
         self.poll_limit = int(t / 200e-9)
+        # "ce": copy-engine all-gather (default); "sm": the SM all-gather kernel
+        self.gather_engine = os.environ.get("NANOSPEC_PEER_GATHER", "ce")
+        # Reduce-scatter: "ce" DMAs the peers' slot ranges into `staging` and sums
+        # locally; "sm" pulls and sums in one SM kernel. Same values either way.
+        self.reduce_engine = os.environ.get("NANOSPEC_PEER_REDUCE", "ce")
+        self.staging = None
+        if self.reduce_engine == "ce":
+            self.staging = torch.empty(self.w.world * max(u.shard_size for u in units), device=self.device,
+                                       dtype=units[0].param.dtype)
+        self.unit_index = {id(u): i for i, u in enumerate(units)}
+        self.pregathered = set()
+        if not serial:
+            # The optimizer calls this after updating each shard: the next step's
+            # gather of that unit starts while the remaining shards are updated.
+            for u in units:
+                u.on_updated = self.publish
         self.active = False
         self.visits = ()
         self.gathered = set()
@@ -127,8 +151,13 @@ class PeerSchedule:
         with torch.cuda.stream(self.stream):
             self._signal(CH_PARAMS)
             self._wait(CH_PARAMS, self.seq[CH_PARAMS])  # every peer's shards are final
-        self.gathered = set()
+        self.gathered, self.pregathered = self.pregathered, set()
         self.active = True
+        if not self.serial:
+            # Gather every unit now, back to back, in visit order: the link never idles
+            # waiting for compute, and compute waits only for the unit it needs.
+            for i in range(len(visits)):
+                self.prefetch(i)
 
     def prefetch(self, index):
         if index >= len(self.visits):
@@ -139,8 +168,27 @@ class PeerSchedule:
             return
         self.gathered.add(key)
         with torch.cuda.stream(self.stream):
-            self.C.peer_allgather(self.w.id, self.w.param_off[key], unit.shard_size, self.resident[key])
+            gather = self.C.peer_allgather_ce if self.gather_engine == "ce" else self.C.peer_allgather
+            gather(self.w.id, self.w.param_off[key], unit.shard_size, self.resident[key])
             self.ready[key].record(self.stream)
+
+    def publish(self, unit):
+        """After this rank's optimizer updated ``unit`` (on the compute stream): flag the
+        unit's parameters as final to every peer and, on the communication stream,
+        gather the unit for the next step once every peer has flagged it too."""
+        if self.active:
+            return  # an update inside a step: the next ``begin`` gathers as usual
+        key = id(unit)
+        ch = CH_UNIT + self.unit_index[key]
+        self.seq.setdefault(ch, 0)
+        self._signal(ch)
+        seq = self.seq[ch]
+        with torch.cuda.stream(self.stream):
+            self._wait(ch, seq)
+            gather = self.C.peer_allgather_ce if self.gather_engine == "ce" else self.C.peer_allgather
+            gather(self.w.id, self.w.param_off[key], unit.shard_size, self.resident[key])
+            self.ready[key].record(self.stream)
+        self.pregathered.add(key)
 
     def acquire(self, index):
         unit = self.visits[index]
@@ -179,7 +227,10 @@ class PeerSchedule:
         self.stream.wait_stream(self.compute)
         with torch.cuda.stream(self.stream):
             self._wait(CH_READY + slot, seq)
-            self.C.peer_reduce_avg(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad)
+            if self.staging is not None:
+                self.C.peer_reduce_avg_ce(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad, self.staging)
+            else:
+                self.C.peer_reduce_avg(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad)
             self._signal(CH_PULLED + slot)
 
     def finish(self):

@@ -122,6 +122,9 @@ def _adamw_cuda(optimizer, den, factor, b1, b2):
                        float(optimizer.weight_decay), float(b1), float(b2), float(optimizer.eps),
                        1.0, 1.0, float(optimizer.max_grad_norm), optimizer._bc, not lazy)
         s.grad_zero = True
+        hook = getattr(s, "on_updated", None)
+        if hook is not None:
+            hook(s)  # e.g. the peer schedule starts the next step's gather of this shard
     norm = norm2.sqrt().reshape(())
     if not optimizer.sync:
         return {"grad_norm": norm, "updated": torch.isfinite(norm), "denominator": den.reshape(())}

@@ -241,6 +241,15 @@ class ShardingPlan:
             sched.close()
         self._cache.clear()
 
+    def parameters_changed(self):
+        """Call after writing parameter shards other than through the optimizer (a
+        checkpoint restore, a manual copy): drops the next-step gathers that the peer
+        schedule started when the optimizer last published the shards."""
+        for key in ("peer", "peer_serial"):
+            sched = self._cache.get(key)
+            if sched is not None:
+                sched.pregathered.clear()
+
     def close_peer(self):
         """Collective: release the peer window (after the last step)."""
         if self.peer_enabled:

@@ -101,6 +101,7 @@ def _schedules(rank, world, outdir):
             s.param.copy_(p0)
             s.master.copy_(s.param)
             s.m.zero_(), s.v.zero_(), s.grad.zero_()
+        m.sharding.parameters_changed()
         opt = N.AdamW(m.sharding, lr=1e-3, weight_decay=0.01)
         rows = []
         for _ in range(3):
