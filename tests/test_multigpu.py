@@ -122,9 +122,12 @@ def _schedules(rank, world, outdir):
     # peer vs NCCL: same math, different reduction order
     for ra, rb in zip(results["nccl_serial"][0], results["peer_serial"][0]):
         assert abs(ra[0] - rb[0]) <= 1e-3 * abs(ra[0])
+    # NCCL's ring reduce-scatter rounds to bf16 after each of its world - 1 additions;
+    # the peer reduce sums in fp32 and rounds once, so the gap grows with the ranks.
+    tol = 1.5e-3 * world
     for x, y in zip(results["nccl_serial"][1], results["peer_serial"][1]):
         rel = ((x.float() - y.float()).norm() / x.float().norm().clamp_min(1e-12)).item()
-        assert rel < 3e-3, rel
+        assert rel < tol, rel
 
 
 @two_gpus
