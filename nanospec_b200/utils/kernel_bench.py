@@ -6,6 +6,14 @@
     python -m nanospec_b200.utils.kernel_bench attention --S 128 --blocks 8
     python -m nanospec_b200.utils.kernel_bench fp8 --T 4096 --k 5120 --nout 17408
     python -m nanospec_b200.utils.kernel_bench gdn --S 4096 --heads 48
+    python -m nanospec_b200.utils.kernel_bench gemm-suite
+
+``gemm-suite`` times every linear product of one draft layer at the benchmark
+shape (forward, input and weight gradients; qwen draft: hidden 5120, FFN 15360,
+8 KV heads x 128, 56 draft and 128 context tokens) against ``torch.matmul``
+(cuBLAS) on the same operands. Each call sequence is captured once in a CUDA
+graph and replayed, so host launch cost is excluded, and weights rotate through
+three copies (> L2).
 
 Each run does ``--warmup`` untimed calls, then times ``--reps`` calls between two
 events on the launching stream. Operands rotate through enough copies to exceed
@@ -136,9 +144,76 @@ def bench_gdn(a):
     return {"op": "gdn_chunk_fwd", "S": s, "heads": nv, "us": round(us, 1)}
 
 
+def _graph_time(fns, reps):
+    """Per-call time of `fns` (one call each) captured in one CUDA graph and replayed."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for f in fns:
+            f()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / (reps * len(fns))
+
+
+def bench_gemm_suite(a):
+    from nanospec_b200 import ops
+    dev, R = "cuda", 3
+    rows = []
+
+    def case(kind, T, nout, k, residual=False):
+        if kind == "wgrad":
+            dy = torch.randn(T, nout, device=dev).bfloat16()
+            x = torch.randn(T, k, device=dev).bfloat16()
+            outs = [torch.empty(nout, k, device=dev, dtype=torch.bfloat16) for _ in range(R)]
+            ours = [lambda o=o: ops.linear_wgrad(dy, x, o) for o in outs]
+            ref = [lambda o=o: torch.matmul(dy.t(), x, out=o) for o in outs]
+        else:
+            ws = [torch.randn(nout, k, device=dev).bfloat16() for _ in range(R)]
+            if kind == "fwd":
+                x = torch.randn(T, k, device=dev).bfloat16()
+                r = torch.randn(T, nout, device=dev).bfloat16() if residual else None
+                outs = [torch.empty(T, nout, device=dev, dtype=torch.bfloat16) for _ in range(R)]
+                ours = [lambda w=w, o=o: ops.linear(x, w, out=o, residual=r) for w, o in zip(ws, outs)]
+                ref = [lambda w=w, o=o: torch.matmul(x, w.t(), out=o) for w, o in zip(ws, outs)]
+            else:
+                dy = torch.randn(T, nout, device=dev).bfloat16()
+                outs = [torch.empty(T, k, device=dev, dtype=torch.bfloat16) for _ in range(R)]
+                ours = [lambda w=w, o=o: ops.linear_dgrad(dy, w, out=o) for w, o in zip(ws, outs)]
+                ref = [lambda w=w, o=o: torch.matmul(dy, w, out=o) for w, o in zip(ws, outs)]
+        o_us, c_us = _graph_time(ours, a.reps), _graph_time(ref, a.reps)
+        wb = 2.0 * nout * k
+        rows.append({"kind": kind, "T": T, "nout": nout, "k": k, "residual": residual, "ours_us": round(o_us, 1),
+                     "cublas_us": round(c_us, 1), "ours_TBps": round(wb / o_us / 1e6, 2),
+                     "cublas_TBps": round(wb / c_us / 1e6, 2)})
+
+    for kind, T, nout, k, res in [("fwd", 56, 5120, 5120, False), ("fwd", 184, 2048, 5120, False),
+                                  ("fwd", 56, 5120, 5120, True), ("fwd", 56, 30720, 5120, False),
+                                  ("fwd", 56, 5120, 15360, True), ("dgrad", 56, 5120, 5120, False),
+                                  ("dgrad", 184, 2048, 5120, False), ("dgrad", 56, 30720, 5120, False),
+                                  ("dgrad", 56, 5120, 15360, False), ("wgrad", 56, 30720, 5120, False),
+                                  ("wgrad", 56, 5120, 15360, False), ("wgrad", 56, 5120, 5120, False),
+                                  ("wgrad", 184, 2048, 5120, False), ("wgrad", 128, 5120, 25600, False)]:
+        case(kind, T, nout, k, res)
+    return {"op": "gemm_suite", "cases": rows, "total_ours_us": round(sum(r["ours_us"] for r in rows), 1),
+            "total_cublas_us": round(sum(r["cublas_us"] for r in rows), 1)}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn"))
+    p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn", "gemm-suite"))
     p.add_argument("--kind", choices=("fwd", "dgrad", "wgrad"), default="fwd")
     p.add_argument("--T", type=int, default=56)
     p.add_argument("--nout", type=int, default=5120)
@@ -155,7 +230,7 @@ def main(argv=None):
     p.add_argument("--rotate", action="store_true", help="rotate operands through > L2 bytes")
     a = p.parse_args(argv)
     fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
-          "fp8": bench_fp8, "gdn": bench_gdn}[a.op]
+          "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite}[a.op]
     print(json.dumps(fn(a)), flush=True)
 
 
