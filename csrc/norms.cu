@@ -55,6 +55,54 @@ __global__ void rms_fwd_kernel(const bf16* __restrict__ x, int64_t ldx, const bf
   }
 }
 
+// Same result as rms_fwd_kernel for rows of n % 8 == 0 elements (n <= 8 * 256 * VPT):
+// the row stays in registers after one pass of 16-byte loads (no second read).
+template <int VPT>
+__global__ void __launch_bounds__(256) rms_fwd_vec_kernel(const bf16* __restrict__ x, int64_t ldx,
+                                                          const bf16* __restrict__ w, bf16* __restrict__ y,
+                                                          int64_t ldy, float* __restrict__ inv_out, int n,
+                                                          float eps) {
+  __shared__ float sh[32];
+  const int64_t row = blockIdx.x;
+  const int n8 = n / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  uint4 xv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = threadIdx.x + v * 256;
+    if (c < n8) xv[v] = xr[c];
+  }
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = threadIdx.x + v * 256;
+    if (c < n8) {
+      const bf16* h = reinterpret_cast<const bf16*>(&xv[v]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f(h[j]) * f(h[j]);
+    }
+  }
+  const float tot = block_sum<256>(ss, sh);
+  const float inv = rsqrtf(tot / n + eps);
+  if (threadIdx.x == 0) inv_out[row] = inv;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * ldy);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int c = threadIdx.x + v * 256;
+    if (c < n8) {
+      const uint4 wv = wr[c];
+      const bf16* h = reinterpret_cast<const bf16*>(&xv[v]);
+      const bf16* wh = reinterpret_cast<const bf16*>(&wv);
+      uint4 o;
+      bf16* oh = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oh[j] = __float2bfloat16(f(wh[j]) * r(f(h[j]) * inv));
+      yr[c] = o;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ RMSNorm backward
 // Blocks take `rows_per_block` rows each; dx per row, dw partial per block.
 __global__ void rms_bwd_kernel(const bf16* __restrict__ dy, int64_t lddy, const bf16* __restrict__ x,
@@ -443,6 +491,24 @@ void rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, at::Tensor y, at::Tens
   NS_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.stride(1) == 1, "rms_norm_fwd: row-major 2-D expected");
   const int rows = x.size(0), n = x.size(1);
   if (rows == 0) return;
+  const bool vec = n % 8 == 0 && n <= 8 * 256 * 4 && x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0;
+  if (vec) {
+    auto launch = [&](auto kern) {
+      kern<<<rows, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0),
+                                       reinterpret_cast<const bf16*>(w.data_ptr()),
+                                       reinterpret_cast<bf16*>(y.data_ptr()), y.stride(0), inv.data_ptr<float>(), n,
+                                       (float)eps);
+    };
+    const int vpt = (n / 8 + 255) / 256;
+    if (vpt <= 1) launch(rms_fwd_vec_kernel<1>);
+    else if (vpt <= 2) launch(rms_fwd_vec_kernel<2>);
+    else launch(rms_fwd_vec_kernel<4>);
+    NS_CUDA(cudaGetLastError());
+    return;
+  }
   rms_fwd_kernel<<<rows, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0),
                                              reinterpret_cast<const bf16*>(w.data_ptr()),
                                              reinterpret_cast<bf16*>(y.data_ptr()), y.stride(0),

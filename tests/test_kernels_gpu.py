@@ -113,7 +113,7 @@ def test_linear_strided_views():
 
 
 @cuda
-@pytest.mark.parametrize("rows,n", [(56, 5120), (7, 64), (300, 1000)])
+@pytest.mark.parametrize("rows,n", [(56, 5120), (7, 64), (300, 1000), (5, 1001)])  # 1001: scalar path
 def test_rms_norm(rows, n):
     x = torch.randn(rows, n, device="cuda").bfloat16()
     w = (1 + 0.1 * torch.randn(n, device="cuda")).bfloat16()
