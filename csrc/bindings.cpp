@@ -8,7 +8,8 @@
 namespace ns {
 void linear(at::Tensor x, at::Tensor w, at::Tensor out, c10::optional<at::Tensor> residual);
 void linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor out, bool accumulate);
-void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate);
+int64_t linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate, c10::optional<at::Tensor> nfac,
+                     c10::optional<at::Tensor> npart, int64_t offset);
 void gemm_test(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int splits);
 void gemm_trace(c10::optional<at::Tensor> buf);
 void rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, at::Tensor y, at::Tensor inv);
@@ -23,6 +24,7 @@ void swiglu_bwd(at::Tensor dp, at::Tensor gu, at::Tensor dgu);
 void embedding_fwd(at::Tensor ids, at::Tensor w, at::Tensor out);
 void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad);
 void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2);
+void grad_norm_sq_ranges(std::vector<at::Tensor> ranges, at::Tensor factor, at::Tensor norm2);
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,
                   at::Tensor factor, at::Tensor norm2, double lr, double wd, double b1, double b2, double eps,
                   double bc1, double bc2, double max_norm, c10::optional<at::Tensor> bc_dev, bool zero_grad);
@@ -67,7 +69,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanospec_b200 sm_100a kernels";
   m.def("linear", &ns::linear);
   m.def("linear_dgrad", &ns::linear_dgrad);
-  m.def("linear_wgrad", &ns::linear_wgrad);
+  m.def("linear_wgrad", &ns::linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("out"), py::arg("accumulate") = false,
+        py::arg("nfac") = py::none(), py::arg("npart") = py::none(), py::arg("offset") = 0);
   m.def("gemm_test", &ns::gemm_test);
   m.def("gemm_trace", &ns::gemm_trace);
   m.def("rms_norm_fwd", &ns::rms_norm_fwd);
@@ -79,6 +82,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &ns::embedding_fwd);
   m.def("embedding_bwd", &ns::embedding_bwd);
   m.def("grad_norm_sq", &ns::grad_norm_sq);
+  m.def("grad_norm_sq_ranges", &ns::grad_norm_sq_ranges);
   m.def("adamw_update", &ns::adamw_update, py::arg("param"), py::arg("master"), py::arg("m"), py::arg("v"),
         py::arg("grad"), py::arg("factor"), py::arg("norm2"), py::arg("lr"), py::arg("wd"), py::arg("b1"),
         py::arg("b2"), py::arg("eps"), py::arg("bc1"), py::arg("bc2"), py::arg("max_norm"),

@@ -52,6 +52,8 @@ struct GemmArgs {
   long long* trace;  // test hook: clock stamps of CTA 0 and per-CTA phase times, or null
   int tma_store;     // persistent kernel: plain bf16 row-major output written by TMA stores
   int cluster_red;   // split-K: the splits of a tile form a cluster and reduce through DSMEM
+  const float* nfac; // with npart: npart[cta] = sum of bf16(out * *nfac)^2 over this CTA's outputs
+  float* npart;
 };
 
 constexpr int CLUSTER_MAX = 8;  // portable cluster size: the largest split count reduced in DSMEM
@@ -151,6 +153,34 @@ __device__ __forceinline__ void store_row32(const GemmArgs& a, int m, int nb, co
     if (a.res) y = sm100::bf16_round(add[j] + y);
     if (a.accumulate) y = sm100::bf16_round(old[j] + y);
     p[j * a.out_sn] = __float2bfloat16(y);
+  }
+}
+
+// Squared-norm contribution of 32 stored bf16 outputs of row m (plain outputs only).
+__device__ __forceinline__ float norm_row32(const GemmArgs& a, int m, int nb, const float (&v)[32], float fac) {
+  float t = 0.f;
+  if (m >= a.M) return t;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (nb + j < a.N) {
+      const float g = sm100::bf16_round(sm100::bf16_round(v[j]) * fac);
+      t += g * g;
+    }
+  return t;
+}
+
+// One float per CTA: the block's sum of the threads' norm contributions, in warp order.
+__device__ __forceinline__ void write_norm_part(const GemmArgs& a, float t, int cta) {
+  __shared__ float red[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    a.npart[cta] = s;
   }
 }
 
@@ -279,6 +309,8 @@ __global__ void __launch_bounds__(192, 1)
   }
   const int q = warp & 3;
   const int m = m0 + q * 32 + lane;
+  const float nf = args.npart ? *args.nfac : 0.f;
+  float nsum = 0.f;
   if (warp >= 2) {
     if (sm100::mbar_wait(acc_full, 0, args.err)) {
       sm100::tc_fence_after();
@@ -312,6 +344,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         } else {
           store_row32(args, m, nb, v);
+          if (args.npart) nsum += norm_row32(args, m, nb, v, nf);
         }
       }
     }
@@ -360,10 +393,25 @@ __global__ void __launch_bounds__(192, 1)
       const int gn = args.ws_t ? n0 + o : n0 + i4;
       if (gm >= args.M || gn >= args.N) continue;
       const int lim = min(4, args.ws_t ? args.M - gm : args.N - gn);
-      if (plain && lim == 4 && ((args.ws_t ? args.out_sm : args.out_sn) == 1) &&
-          ((args.ws_t ? args.out_sn : args.out_sm) % 4 == 0)) {
+      const bool contig = lim == 4 && ((args.ws_t ? args.out_sm : args.out_sn) == 1) &&
+                          ((args.ws_t ? args.out_sn : args.out_sm) % 4 == 0) &&
+                          reinterpret_cast<uintptr_t>(args.out) % 8 == 0;
+      if (plain && contig) {
         __nv_bfloat162 h[2] = {__floats2bfloat162_rn(acc[0], acc[1]), __floats2bfloat162_rn(acc[2], acc[3])};
         *reinterpret_cast<uint2*>(args.out + gm * args.out_sm + gn * args.out_sn) = *reinterpret_cast<uint2*>(h);
+        continue;
+      }
+      if (contig && args.res && !args.out_f32 && !args.accumulate &&
+          ((args.ws_t ? args.res_sm : args.res_sn) == 1) && ((args.ws_t ? args.res_sn : args.res_sm) % 4 == 0) &&
+          reinterpret_cast<uintptr_t>(args.res) % 8 == 0) {
+        // y = bf16(res + bf16(acc)) for 4 contiguous outputs, 8-byte loads and stores
+        const uint2 rv = *reinterpret_cast<const uint2*>(args.res + gm * args.res_sm + gn * args.res_sn);
+        const __nv_bfloat16* rh = reinterpret_cast<const __nv_bfloat16*>(&rv);
+        __nv_bfloat16 o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          o[e] = __float2bfloat16(__bfloat162float(rh[e]) + sm100::bf16_round(acc[e]));
+        *reinterpret_cast<uint2*>(args.out + gm * args.out_sm + gn * args.out_sn) = *reinterpret_cast<uint2*>(o);
         continue;
       }
       float add[4], old[4];
@@ -464,6 +512,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   stamp(4);
+  if (args.npart) write_norm_part(args, nsum, cta_id);
 }
 
 // Persistent variant for grids with more tiles than SMs (no split-K): one CTA per SM
@@ -527,6 +576,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  float nsum = 0.f;  // norm side output (epilogue threads)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -599,6 +649,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;
     uint8_t* stg = sE + q * 2 * EPI_BOX_BYTES;
+    const float nf = args.npart ? *args.nfac : 0.f;
     int local = 0, box = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -626,6 +677,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(src[2 * t], src[2 * t + 1]);
             *reinterpret_cast<uint4*>(sb + lane * 128 + ((j ^ (lane & 7)) * 16)) = *reinterpret_cast<uint4*>(h);
+            if (args.npart) {
+              // from the stored bf16 values; rows >= M and columns >= N are exact zeros
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float2 hv = __bfloat1622float2(h[t]);
+                const float a = sm100::bf16_round(hv.x * nf), b = sm100::bf16_round(hv.y * nf);
+                nsum = fmaf(a, a, fmaf(b, b, nsum));
+              }
+            }
           }
           sm100::fence_proxy_async_smem();
           __syncwarp();
@@ -639,7 +699,10 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < BN; c += 32) {
           float v[32];
           sm100::tmem_ld32(trow + (uint32_t)c, v);
-          if (m < args.M && n0 + c < args.N) store_row32(args, m, n0 + c, v);
+          if (m < args.M && n0 + c < args.N) {
+            store_row32(args, m, n0 + c, v);
+            if (args.npart) nsum += norm_row32(args, m, n0 + c, v, nf);
+          }
         }
       }
       sm100::tc_fence_before();
@@ -654,6 +717,7 @@ __global__ void __launch_bounds__(192, 1)
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, P::TMEM_COLS);
   }
+  if (args.npart) write_norm_part(args, nsum, blockIdx.x);
 }
 
 template <int BN, bool AMN, bool BMN>
@@ -778,7 +842,70 @@ struct GemmPlan {
   bool persistent;
 };
 
-static GemmPlan plan_gemm(int M, int N, int K, int force_splits) {
+// How many clusters of `s` split CTAs (one tile each) the GPU runs at once: clusters
+// must fit inside one GPC, so for large `s` this is less than SMs / s. Queried from
+// the runtime once per (kernel, cluster size, shared memory) and cached.
+template <int BN, bool AMN, bool BMN>
+static int max_active_clusters(int s, int smem) {
+  static std::map<std::pair<int, int>, int> cache;
+  const auto key = std::make_pair(s, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kern = gemm_bf16_kernel<BN, AMN, BMN>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM_MAX) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, s);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a failed query only means "unknown": fall back below
+  if (n <= 0) n = std::max(1, num_sms() / s);
+  cache[key] = n;
+  return n;
+}
+
+static int max_active_clusters(int bn, bool amn, bool bmn, int s, int smem) {
+#define NS_MAC(B)                                                              \
+  if (bn == B) {                                                               \
+    if (!amn && !bmn) return max_active_clusters<B, false, false>(s, smem);   \
+    if (amn && !bmn) return max_active_clusters<B, true, false>(s, smem);     \
+    if (!amn && bmn) return max_active_clusters<B, false, true>(s, smem);     \
+    return max_active_clusters<B, true, true>(s, smem);                       \
+  }
+  NS_MAC(64)
+  NS_MAC(128)
+  NS_MAC(192)
+  NS_MAC(256)
+#undef NS_MAC
+  return std::max(1, num_sms() / s);
+}
+
+// Dynamic shared memory of a split-K (solo) launch, as launch_bn computes it.
+static int solo_smem(int bn, int kpb, bool cluster) {
+  const int stages = std::max(1, std::min(max_stages(bn, true), kpb));
+  int stage_bytes = 0, tmem_cols = 0, smem_max = 0;
+  switch (bn) {
+    case 64: stage_bytes = GemmCfg<64>::STAGE_BYTES; tmem_cols = GemmCfg<64>::TMEM_COLS; smem_max = GemmCfg<64>::SMEM_MAX; break;
+    case 128: stage_bytes = GemmCfg<128>::STAGE_BYTES; tmem_cols = GemmCfg<128>::TMEM_COLS; smem_max = GemmCfg<128>::SMEM_MAX; break;
+    case 192: stage_bytes = GemmCfg<192>::STAGE_BYTES; tmem_cols = GemmCfg<192>::TMEM_COLS; smem_max = GemmCfg<192>::SMEM_MAX; break;
+    default: stage_bytes = GemmCfg<256>::STAGE_BYTES; tmem_cols = GemmCfg<256>::TMEM_COLS; smem_max = GemmCfg<256>::SMEM_MAX; break;
+  }
+  const int min_smem = (228 * 1024) / (512 / tmem_cols + 1) - 1024 + 64;
+  const int ring = stages * stage_bytes;
+  const int used = (cluster ? std::max(ring, partial_bytes(bn)) : ring) + 1024 + 256;
+  return std::max(used, std::min(min_smem, smem_max));
+}
+
+static GemmPlan plan_gemm(int M, int N, int K, int force_splits, bool amn = false, bool bmn = false) {
   const int sms = num_sms();
   auto base = [&](int bn) {
     GemmPlan p{};
@@ -829,7 +956,12 @@ static GemmPlan plan_gemm(int M, int N, int K, int force_splits) {
       const double t_fix = s == 1 ? 0.0
                            : dsmem ? RED_FIXED + (double)BM * bn * 4 / RED_BW
                                    : s * (double)BM * bn * 4 / FIX_BW;
-      const double cost = std::max(t_main, t_hbm) + t_fix;
+      // clusters that do not all fit at once run in waves
+      const int waves = (s > 1 && dsmem)
+                            ? (tiles + max_active_clusters(bn, amn, bmn, s, solo_smem(bn, kpb, true)) - 1) /
+                                  max_active_clusters(bn, amn, bmn, s, solo_smem(bn, kpb, true))
+                            : 1;
+      const double cost = std::max(waves * t_main, t_hbm) + waves * t_fix;
       if (cost < best_cost * 0.98) {
         best_cost = cost;
         best = finish(p, s);
@@ -840,9 +972,14 @@ static GemmPlan plan_gemm(int M, int N, int K, int force_splits) {
 }
 
 // D[M,N] = A * B^T with the epilogue `e`.
-void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e, int force_splits) {
+int gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e, int force_splits) {
   NS_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
-  const GemmPlan plan = plan_gemm(M, N, K, force_splits);
+  if (e.npart) {
+    NS_CHECK(e.nfac && e.out && !e.out_f32 && !e.res && !e.accumulate,
+             "the norm side output needs a plain bf16 output");
+    if (force_splits == 0) force_splits = 1;  // one CTA stores each element
+  }
+  const GemmPlan plan = plan_gemm(M, N, K, force_splits, A.mn_major, B.mn_major);
   const int bn = plan.bn, bk = plan.bk, mt = plan.mt, nt = plan.nt;
   const int tiles = mt * nt;
   const int splits = plan.splits, kpb = plan.kpb;
@@ -870,6 +1007,8 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
   a.err = device_error_flag();
   a.trace = g_trace;
   a.ws_t = (e.sn != 1) ? 1 : 0;
+  a.nfac = e.nfac;
+  a.npart = e.npart;
   // split-K reduces in DSMEM within a cluster; a count above the portable cluster
   // size uses fp32 partials in global memory and a last-CTA fix-up
   a.cluster_red = (splits > 1 && splits <= CLUSTER_MAX && !g_trace) ? 1 : 0;
@@ -890,13 +1029,14 @@ void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const 
     else if (A.mn_major && !B.mn_major) launch_persistent<true, false>(bn, ta, tb, to, a, mt, tiles);
     else if (!A.mn_major && B.mn_major) launch_persistent<false, true>(bn, ta, tb, to, a, mt, tiles);
     else launch_persistent<true, true>(bn, ta, tb, to, a, mt, tiles);
-    return;
+    return std::min(tiles, num_sms());
   }
   dim3 grid(mt, nt, splits);
   if (!A.mn_major && !B.mn_major) launch<false, false>(bn, ta, tb, a, grid, stages);
   else if (A.mn_major && !B.mn_major) launch<true, false>(bn, ta, tb, a, grid, stages);
   else if (!A.mn_major && B.mn_major) launch<false, true>(bn, ta, tb, a, grid, stages);
   else launch<true, true>(bn, ta, tb, a, grid, stages);
+  return tiles * splits;
 }
 
 // ----------------------------------------------------------------------------- torch API
@@ -949,8 +1089,11 @@ void linear_dgrad(at::Tensor dy, at::Tensor w, at::Tensor out, bool accumulate) 
   }
 }
 
-// dW[Nout, K] (+)= dy[T, Nout]^T @ x[T, K]
-void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate) {
+// dW[Nout, K] (+)= dy[T, Nout]^T @ x[T, K]. With `nfac`/`npart` (plain output only),
+// also writes this launch's per-CTA partials of sum bf16(dW * nfac)^2 to
+// npart[offset, offset + returned count).
+int64_t linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate, c10::optional<at::Tensor> nfac,
+                     c10::optional<at::Tensor> npart, int64_t offset) {
   check_rowmajor(dy, "dy");
   check_rowmajor(x, "x");
   check_bf16(out, "out");
@@ -960,8 +1103,15 @@ void linear_wgrad(at::Tensor dy, at::Tensor x, at::Tensor out, bool accumulate) 
   const int64_t ld = out.dim() == 2 ? out.stride(0) : K;
   Operand A{dy.data_ptr(), T, Nout, dy.stride(0), true};  // A[m=nout, r=t] = dy[t, nout]
   Operand B{x.data_ptr(), T, K, x.stride(0), true};       // B[n=k, r=t] = x[t, k]
-  gemm_launch(A, B, Nout, K, T,
-              Epilogue{reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr, ld, 1, nullptr, 0, 0, accumulate});
+  Epilogue e{reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr, ld, 1, nullptr, 0, 0, accumulate};
+  if (npart && npart->defined()) {
+    NS_CHECK(nfac && nfac->defined() && nfac->scalar_type() == at::kFloat && npart->scalar_type() == at::kFloat,
+             "linear_wgrad: fp32 norm factor and partial buffer expected");
+    NS_CHECK(offset >= 0 && offset + num_sms() <= npart->numel(), "linear_wgrad: norm partial buffer full");
+    e.nfac = nfac->data_ptr<float>();
+    e.npart = npart->data_ptr<float>() + offset;
+  }
+  return gemm_launch(A, B, Nout, K, T, e);
 }
 
 // Test hook: record clock64 stamps (TMA issue [0,256), MMA start [256,512)) of CTA 0

@@ -17,6 +17,10 @@ struct Operand {
 // Epilogue of D[m, n]: exactly one of `out` (bf16) / `out_f32` is set. Element
 // (m, n) lives at m * sm + n * sn. bf16: out = bf16(res + bf16(D)) (+ old out when
 // accumulate). fp32: out_f32 = D (+ old value when accumulate).
+//
+// Optional squared-norm side output (plain bf16 outputs only, no split-K): with
+// `npart` set, every CTA writes npart[cta] = sum over the elements it stored of
+// bf16(out * factor)^2, factor = *nfac; the caller sums the partials in order.
 struct Epilogue {
   __nv_bfloat16* out;
   float* out_f32;
@@ -24,10 +28,13 @@ struct Epilogue {
   const __nv_bfloat16* res;
   int64_t rsm, rsn;
   bool accumulate;
+  const float* nfac = nullptr;
+  float* npart = nullptr;
 };
 
 // D[M, N] = sum_k A[m, k] B[n, k] on tcgen05; force_splits > 0 fixes the split-K count.
-void gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e,
-                 int force_splits = 0);
+// Returns the number of CTAs launched (the norm partials written when requested).
+int gemm_launch(const Operand& A, const Operand& B, int M, int N, int K, const Epilogue& e,
+                int force_splits = 0);
 
 }  // namespace ns

@@ -4,6 +4,8 @@
 // and round again), so the kernels agree with the CPU path to bf16 resolution.
 // Weight-gradient column sums use per-block partials plus a fixed-order final
 // reduction: results are bitwise reproducible run to run.
+#include <vector>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -345,6 +347,15 @@ __global__ void grad_norm_part_kernel(const bf16* __restrict__ g, int64_t n, con
   __shared__ float sh[32];
   const float fac = *factor;
   float s = 0.f;
+  // elements before the first 16-byte boundary (ranges inside a shard), then 8 at a time
+  const int64_t lead_want = (int64_t)(((16 - (reinterpret_cast<uintptr_t>(g) & 15)) & 15) / 2);
+  const int64_t lead = n < lead_want ? n : lead_want;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < lead; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = r(f(g[i]) * fac);
+    s += v * v;
+  }
+  g += lead;
+  n -= lead;
   const int64_t n8 = n / 8;
   const uint4* g8 = reinterpret_cast<const uint4*>(g);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
@@ -357,6 +368,55 @@ __global__ void grad_norm_part_kernel(const bf16* __restrict__ g, int64_t n, con
     }
   }
   for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = r(f(g[i]) * fac);
+    s += v * v;
+  }
+  const float t = block_sum<256>(s, sh);
+  if (threadIdx.x == 0) part[blockIdx.x] = t;
+}
+
+// The same squared norm over up to NR separate gradient ranges in one launch: block
+// b works on range r with block_start[r] <= b < block_start[r + 1] (host-assigned in
+// proportion to the range sizes) and writes part[b].
+constexpr int NR = 64;
+struct NormRanges {
+  const bf16* p[NR];
+  int64_t n[NR];
+  int block_start[NR + 1];
+  int count;
+};
+
+__global__ void grad_norm_ranges_kernel(NormRanges rs, const float* __restrict__ factor, float* __restrict__ part) {
+  __shared__ float sh[32];
+  int ri = 0;
+  while (ri + 1 < rs.count && (int)blockIdx.x >= rs.block_start[ri + 1]) ++ri;
+  const int lb = blockIdx.x - rs.block_start[ri], nb = rs.block_start[ri + 1] - rs.block_start[ri];
+  const float fac = *factor;
+  const bf16* g = rs.p[ri];
+  int64_t n = rs.n[ri];
+  float s = 0.f;
+  const int64_t lead_want = (int64_t)(((16 - (reinterpret_cast<uintptr_t>(g) & 15)) & 15) / 2);
+  const int64_t lead = n < lead_want ? n : lead_want;
+  const int64_t stride = (int64_t)nb * blockDim.x;
+  const int64_t t0 = (int64_t)lb * blockDim.x + threadIdx.x;
+  for (int64_t i = t0; i < lead; i += stride) {
+    const float v = r(f(g[i]) * fac);
+    s += v * v;
+  }
+  g += lead;
+  n -= lead;
+  const int64_t n8 = n / 8;
+  const uint4* g8 = reinterpret_cast<const uint4*>(g);
+  for (int64_t i = t0; i < n8; i += stride) {
+    const uint4 raw = g8[i];
+    const bf16* h = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = r(f(h[j]) * fac);
+      s += v * v;
+    }
+  }
+  for (int64_t i = n8 * 8 + t0; i < n; i += stride) {
     const float v = r(f(g[i]) * fac);
     s += v * v;
   }
@@ -649,7 +709,8 @@ void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad) {
 
 void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2) {
   const int64_t n = grad.numel();
-  NS_CHECK(reinterpret_cast<uintptr_t>(grad.data_ptr()) % 16 == 0, "grad_norm_sq: 16-byte aligned shard expected");
+  NS_CHECK(reinterpret_cast<uintptr_t>(grad.data_ptr()) % 2 == 0, "grad_norm_sq: bf16 gradient expected");
+  if (n == 0) return;
   const int blocks = (int)std::min<int64_t>(num_sms() * 4, std::max<int64_t>(1, (n / 8 + 255) / 256));
   auto part = at::empty({blocks}, grad.options().dtype(at::kFloat));
   grad_norm_part_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(grad.data_ptr()), n,
@@ -657,6 +718,33 @@ void grad_norm_sq(at::Tensor grad, at::Tensor factor, at::Tensor norm2) {
   NS_CUDA(cudaGetLastError());
   sum_into_kernel<<<1, 32, 0, stream()>>>(part.data_ptr<float>(), blocks, norm2.data_ptr<float>());
   NS_CUDA(cudaGetLastError());
+}
+
+// norm2 += sum over every range of sum bf16(g * factor)^2 (one launch per 64 ranges).
+void grad_norm_sq_ranges(std::vector<at::Tensor> ranges, at::Tensor factor, at::Tensor norm2) {
+  for (size_t base = 0; base < ranges.size(); base += NR) {
+    NormRanges rs{};
+    rs.count = 0;
+    int blocks = 0;
+    for (size_t i = base; i < ranges.size() && rs.count < NR; ++i) {
+      const at::Tensor& g = ranges[i];
+      check_bf16(g, "gradient range");
+      NS_CHECK(g.is_contiguous(), "gradient ranges must be contiguous");
+      if (g.numel() == 0) continue;
+      rs.p[rs.count] = reinterpret_cast<const bf16*>(g.data_ptr());
+      rs.n[rs.count] = g.numel();
+      rs.block_start[rs.count] = blocks;
+      blocks += (int)std::min<int64_t>(num_sms() * 2, std::max<int64_t>(1, (g.numel() / 8 + 255) / 256));
+      ++rs.count;
+    }
+    if (rs.count == 0) continue;
+    rs.block_start[rs.count] = blocks;
+    auto part = at::empty({blocks}, norm2.options());
+    grad_norm_ranges_kernel<<<blocks, 256, 0, stream()>>>(rs, factor.data_ptr<float>(), part.data_ptr<float>());
+    NS_CUDA(cudaGetLastError());
+    sum_into_kernel<<<1, 32, 0, stream()>>>(part.data_ptr<float>(), blocks, norm2.data_ptr<float>());
+    NS_CUDA(cudaGetLastError());
+  }
 }
 
 void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor grad,

@@ -19,6 +19,8 @@ Execution differs from the reference in layout, not in math:
 
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 
 import torch
@@ -120,6 +122,12 @@ class DraftStep:
         sched = plan.schedule(overlap=overlap, resident=resident)
         nl = len(plan.layers)
         visit = 0
+        # One rank, one micro-step, every shard's gradient written in place: the
+        # weight-gradient GEMMs can also produce the optimizer's gradient norm.
+        fuse_norm = (ids.is_cuda and plan.context.world_size == 1 and accumulation_steps == 1
+                     and os.environ.get("NANOSPEC_FUSED_NORM", "1") != "0"
+                     and all(getattr(u, "grad_zero", False) for u in plan))
+        self.norm = None
 
         if loss_mask is None:
             loss_mask = torch.ones(b, s, dtype=torch.float32, device=ids.device)
@@ -211,6 +219,10 @@ class DraftStep:
             hidden, m.lm_head.weight, e, markov.markov_w2.weight if markov is not None else None,
             prep, o, dw2_out=g["markov_head.markov_w2.weight"] if markov is not None else None,
             accumulation_steps=accumulation_steps, **kwargs)
+        if fuse_norm:
+            from .parallel.optim import FusedGradNorm, step_factor
+            den = metrics.denominator.detach().clone().float().reshape(())
+            self.norm = FusedGradNorm(step_factor(den, 1, accumulation_steps))
         if markov is not None:
             ops.embedding_backward(de, prep.previous.reshape(-1), g["markov_head.markov_w1.weight"])
         dx = ops.rms_norm_backward(dh, x, inv_f, m.final_norm.weight, g["final_norm.weight"])
@@ -224,20 +236,21 @@ class DraftStep:
             unit = sched.acquire(visit)
             sched.prefetch(visit + 1)
             g = _bind_grads(sched, visit, unit)
+            nrm = self.norm.bind(unit) if self.norm is not None else None
             sv = saved.pop()
             attn, mlp = layer.self_attn, layer.mlp
             dp = ops.linear_dgrad(dx, mlp.down_proj.weight)
-            ops.linear_wgrad(dx, sv["prod"], g["mlp.down_proj.weight"])
+            ops.linear_wgrad(dx, sv["prod"], g["mlp.down_proj.weight"], norm=nrm)
             dgu = ops.swiglu_backward(dp, sv["gu"])
             del dp
             dn2 = ops.linear_dgrad(dgu, _span(unit, "mlp.gate_proj.weight", "mlp.up_proj.weight"))
-            ops.linear_wgrad(dgu, sv["n2"], g.span("mlp.gate_proj.weight", "mlp.up_proj.weight"))
+            ops.linear_wgrad(dgu, sv["n2"], g.span("mlp.gate_proj.weight", "mlp.up_proj.weight"), norm=nrm)
             del dgu
             dr = ops.rms_norm_backward(dn2, sv["x1"], sv["inv_2"], layer.post_attention_layernorm.weight,
                                        g["post_attention_layernorm.weight"], residual=dx)
             del dn2
             da = ops.linear_dgrad(dr, attn.o_proj.weight)
-            ops.linear_wgrad(dr, sv["a_out"].reshape(b * td, qd), g["self_attn.o_proj.weight"])
+            ops.linear_wgrad(dr, sv["a_out"].reshape(b * td, qd), g["self_attn.o_proj.weight"], norm=nrm)
             dkv = torch.empty_like(sv["kv"])
             dk_rot = torch.empty(b * (s + td), hk, d, device=x.device, dtype=dtype)
             dq_rot, _, _ = ops.attention_backward(
@@ -255,13 +268,14 @@ class DraftStep:
             del dq_rot, dk_rot
             wkv = _span(unit, "self_attn.k_proj.weight", "self_attn.v_proj.weight")
             dxin = ops.linear_dgrad(dkv, wkv)
-            ops.linear_wgrad(dkv, sv["xin"], g.span("self_attn.k_proj.weight", "self_attn.v_proj.weight"))
+            ops.linear_wgrad(dkv, sv["xin"], g.span("self_attn.k_proj.weight", "self_attn.v_proj.weight"),
+                              norm=nrm)
             del dkv
             dq2 = dq.reshape(b * td, qd)
             n = sv["xin"][b * s:]
             dn = dxin[b * s:]
             ops.linear_dgrad(dq2, attn.q_proj.weight, out=dn, accumulate=True)
-            ops.linear_wgrad(dq2, n, g["self_attn.q_proj.weight"])
+            ops.linear_wgrad(dq2, n, g["self_attn.q_proj.weight"], norm=nrm)
             del dq, dq2
             dx = ops.rms_norm_backward(dn, sv["x"], sv["inv_in"], layer.input_layernorm.weight,
                                        g["input_layernorm.weight"], residual=dr)
@@ -275,7 +289,8 @@ class DraftStep:
         g = _bind_grads(sched, visit, unit)
         dproj = ops.rms_norm_backward(dc, projected, inv_ctx, m.context_norm.weight,
                                       g["context_norm.weight"])
-        ops.linear_wgrad(dproj, context_input, g["context_proj.weight"])
+        ops.linear_wgrad(dproj, context_input, g["context_proj.weight"],
+                          norm=self.norm.bind(unit) if self.norm is not None else None)
         if m.fc_norm:
             dcat = ops.linear_dgrad(dproj, m.context_proj.weight)
             width = c.target_hidden_size
@@ -328,5 +343,5 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
     update = None
     if optimizer is not None:
         from .parallel.optim import adamw_step
-        update = adamw_step(optimizer, metrics.denominator, accumulation_steps)
+        update = adamw_step(optimizer, metrics.denominator, accumulation_steps, fused_norm=step.norm)
     return TrainResult(teacher_batch, metrics, hidden, update)

@@ -60,10 +60,19 @@ def linear_dgrad(dy, w, out=None, accumulate=False):
     return dx
 
 
-def linear_wgrad(dy, x, out, accumulate=False):
-    """``out (+)= dy^T @ x`` over all leading dims. out [N, K] in compute dtype."""
+def linear_wgrad(dy, x, out, accumulate=False, norm=None):
+    """``out (+)= dy^T @ x`` over all leading dims. out [N, K] in compute dtype.
+
+    ``norm``: a ``parallel.optim.FusedGradNorm`` bound to the shard that owns ``out``
+    (``FusedGradNorm.bind(shard)``); the GEMM then also writes its part of the
+    squared gradient norm while it stores ``out`` (CUDA, plain overwrite only).
+    """
     if dy.is_cuda:
-        _c().linear_wgrad(dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1]), out, accumulate)
+        dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
+        if norm is not None and not accumulate:
+            norm.launch(lambda f, part, off: _c().linear_wgrad(dy2, x2, out, False, f, part, off), out)
+        else:
+            _c().linear_wgrad(dy2, x2, out, accumulate)
         return out
     dw = ref.linear_wgrad(dy, x)
     if accumulate:

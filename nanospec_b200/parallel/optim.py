@@ -65,6 +65,71 @@ class AdamW:
             self._dev_step.fill_(int(value))
 
 
+def step_factor(den, world, accumulation_steps):
+    """``N * accumulation_steps / den`` (0 when den == 0): the optimizer's gradient scale."""
+    return torch.where(den > 0, world * accumulation_steps / den.clamp_min(1e-6), torch.zeros_like(den))
+
+
+class FusedGradNorm:
+    """Squared gradient norm collected by the weight-gradient GEMMs while they write.
+
+    One training rank only (the norm is over the final gradient, which with N > 1
+    exists only after the reduce-scatter). The GEMM epilogues write per-CTA partials
+    of sum bf16(grad * factor)^2 into ``part`` in launch order; ``norm2`` adds them
+    in that order and runs the ordinary norm kernel over every gradient range no
+    GEMM covered (norm weights, embeddings, the Markov head), so the result is
+    deterministic and no second pass reads the GEMM-written gradients.
+    """
+
+    CAPACITY = 1 << 16
+
+    def __init__(self, factor):
+        self.factor = factor.reshape(1).contiguous()
+        self.part = torch.empty(self.CAPACITY, device=factor.device, dtype=torch.float32)
+        self.offset = 0
+        self.covered = {}
+        self.ok = True
+
+    def bind(self, shard):
+        return _BoundNorm(self, shard)
+
+    def norm2(self, shards, factor):
+        """Global squared norm (1-element fp32 tensor) for ``shards``; ``factor`` must
+        equal the one the GEMMs used (same ``step_factor`` inputs)."""
+        C = cuda_ops()
+        n2 = self.part[:self.offset].sum().reshape(1) if self.offset else torch.zeros(
+            1, device=factor.device, dtype=torch.float32)
+        ranges = []
+        for s in shards:
+            start = 0
+            for a, b in sorted(self.covered.get(id(s), ())):
+                if a > start:
+                    ranges.append(s.grad[start:a])
+                start = max(start, b)
+            if start < s.grad.numel():
+                ranges.append(s.grad[start:])
+        if ranges:
+            C.grad_norm_sq_ranges(ranges, factor, n2)
+        return n2
+
+
+class _BoundNorm:
+    def __init__(self, acc, shard):
+        self.acc, self.shard = acc, shard
+
+    def launch(self, gemm, out):
+        acc, grad = self.acc, self.shard.grad
+        start = (out.data_ptr() - grad.data_ptr()) // grad.element_size()
+        inside = 0 <= start and start + out.numel() <= grad.numel() and out.is_contiguous()
+        if not acc.ok or not inside or acc.offset + 1024 > acc.CAPACITY:
+            acc.ok = False
+            gemm(None, None, 0)
+            return
+        used = gemm(acc.factor, acc.part, acc.offset)
+        acc.offset += int(used)
+        acc.covered.setdefault(id(self.shard), []).append((start, start + out.numel()))
+
+
 def zero_grad(optimizer):
     for s in optimizer.shards:
         s.grad.zero_()
@@ -72,16 +137,19 @@ def zero_grad(optimizer):
 
 
 @torch.no_grad()
-def adamw_step(optimizer, local_denominator, accumulation_steps=1):
+def adamw_step(optimizer, local_denominator, accumulation_steps=1, fused_norm=None):
+    """``fused_norm``: a ``FusedGradNorm`` filled during this step's backward (one rank,
+    CUDA); it replaces the separate squared-norm pass over the gradients."""
     first = optimizer.shards[0]
     den = local_denominator.detach().clone().float().reshape(())
     if first.world_size > 1:
         dist.all_reduce(den, group=first.group)
-    factor = torch.where(den > 0, first.world_size * accumulation_steps / den.clamp_min(1e-6),
-                         torch.zeros_like(den))
+    factor = step_factor(den, first.world_size, accumulation_steps)
     b1, b2 = optimizer.betas
     if first.param.is_cuda:
-        return _adamw_cuda(optimizer, den, factor, b1, b2)
+        if fused_norm is not None and (first.world_size != 1 or not fused_norm.ok):
+            fused_norm = None
+        return _adamw_cuda(optimizer, den, factor, b1, b2, fused_norm)
     norm2 = torch.zeros_like(den)
     for s in optimizer.shards:
         norm2 += ref.scaled_grad(s.grad, factor).square().sum()
@@ -101,14 +169,17 @@ def adamw_step(optimizer, local_denominator, accumulation_steps=1):
     return {"grad_norm": float(norm), "updated": True, "denominator": float(den)}
 
 
-def _adamw_cuda(optimizer, den, factor, b1, b2):
+def _adamw_cuda(optimizer, den, factor, b1, b2, fused_norm=None):
     C = cuda_ops()
     first = optimizer.shards[0]
     # norm2 and the update both consume factor from device memory: no host sync.
-    norm2 = torch.zeros(1, device=den.device, dtype=torch.float32)
     f = factor.reshape(1).contiguous()
-    for s in optimizer.shards:
-        C.grad_norm_sq(s.grad, f, norm2)
+    if fused_norm is not None:
+        norm2 = fused_norm.norm2(optimizer.shards, f)
+    else:
+        norm2 = torch.zeros(1, device=den.device, dtype=torch.float32)
+        for s in optimizer.shards:
+            C.grad_norm_sq(s.grad, f, norm2)
     if first.world_size > 1:
         dist.all_reduce(norm2, group=first.group)
     if optimizer._dev_step is None:

@@ -299,3 +299,38 @@ def test_adamw_nonfinite_skips():
     assert r["updated"] is False and opt.steps == 0
     assert torch.equal(u.master, torch.ones(1000, device="cuda"))
     assert u.grad.abs().max().item() == 0
+
+
+@cuda
+@pytest.mark.parametrize("nout,k", [(2560, 3072), (96, 200)])  # persistent / single-wave kernels
+def test_wgrad_norm_side_output(nout, k):
+    # Per-CTA partials of sum bf16(dW * f)^2 written by the GEMM equal the norm pass over dW.
+    T = 56
+    dy = torch.randn(T, nout, device="cuda").bfloat16()
+    x = torch.randn(T, k, device="cuda").bfloat16()
+    out = torch.empty(nout, k, device="cuda", dtype=torch.bfloat16)
+    f = torch.tensor([0.37], device="cuda")
+    part = torch.full((4096,), float("nan"), device="cuda")
+    used = C().linear_wgrad(dy, x, out, False, f, part, 5)
+    assert 0 < used <= 148 * 4
+    close(out, dy.float().t() @ x.float())
+    ref = torch.zeros(1, device="cuda")
+    C().grad_norm_sq(out.reshape(-1), f, ref)
+    got = part[5:5 + used].sum().item()
+    assert abs(got - ref.item()) <= 1e-5 * ref.item(), (got, ref.item())
+
+
+@cuda
+def test_grad_norm_ranges_matches_per_range():
+    g = torch.randn(300001, device="cuda").bfloat16()
+    f = torch.tensor([1.7], device="cuda")
+    ranges = [g[3:1000], g[1000:1001], g[5000:250007], g[250007:]]  # unaligned starts, a 1-element range
+    a = torch.zeros(1, device="cuda")
+    C().grad_norm_sq_ranges(ranges, f, a)
+    b = torch.zeros(1, device="cuda")
+    for r in ranges:
+        C().grad_norm_sq(r, f, b)
+    ref = (g[3:].float() * 1.7).bfloat16().float().square().sum().item() - \
+        (g[1001:5000].float() * 1.7).bfloat16().float().square().sum().item()
+    assert abs(a.item() - b.item()) <= 1e-5 * b.item()
+    assert abs(a.item() - ref) <= 1e-4 * ref

@@ -127,3 +127,29 @@ def test_lazy_zero_matches_eager_zero():
     assert runs[0][0] == runs[1][0]
     for a, b in zip(runs[0][1], runs[1][1]):
         assert torch.equal(a, b)
+
+
+@cuda
+def test_fused_grad_norm_matches_separate_pass():
+    # The norm written by the weight-gradient GEMM epilogues (+ the uncovered ranges)
+    # equals the separate squared-norm pass over the same gradients.
+    from nanospec_b200.ops._ext import cuda_ops
+    from nanospec_b200.parallel.optim import step_factor
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    o = N.Objective(num_anchors=8)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    ids = torch.randint(0, c.vocab_size, (1, 128), device="cuda", generator=g)
+    hs = [torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16() for _ in range(2)]
+    last = torch.randn(1, 128, c.hidden_size, device="cuda", generator=g).bfloat16()
+    m = _model(c, "cuda", torch.bfloat16)
+    torch.manual_seed(4)
+    r = N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last))
+    fused = m._draft_step.norm
+    assert fused is not None and fused.ok and fused.offset > 0
+    den = r.metrics.denominator.detach().clone().float().reshape(())
+    f = step_factor(den, 1, 1).reshape(1).contiguous()
+    a = fused.norm2(list(m.sharding), f)
+    b = torch.zeros(1, device="cuda")
+    for s in m.sharding:
+        cuda_ops().grad_norm_sq(s.grad, f, b)
+    assert abs(a.item() - b.item()) <= 1e-5 * b.item(), (a.item(), b.item())
