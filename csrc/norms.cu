@@ -463,7 +463,7 @@ __device__ __forceinline__ void adam_one(float g, float& w, float& mm, float& vv
 // guarantees the next backward overwrites every element). 4 elements per thread per iteration
 // (16-byte fp32 and 8-byte bf16 accesses). Skips the update (but still zeroes the
 // gradient) when the global norm in device memory is not finite.
-__global__ void __launch_bounds__(256) adamw_kernel(bf16* __restrict__ param, float* __restrict__ master,
+__global__ void __launch_bounds__(256, 4) adamw_kernel(bf16* __restrict__ param, float* __restrict__ master,
                                                     float* __restrict__ m, float* __restrict__ v,
                                                     bf16* __restrict__ grad, int64_t n,
                                                     const float* __restrict__ factor,
@@ -756,7 +756,9 @@ void adamw_update(at::Tensor param, at::Tensor master, at::Tensor m, at::Tensor 
            "adamw: shard buffers must be 16/8-byte aligned");
   AdamHyper h{(float)lr, (float)wd, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2, (float)max_norm,
               bc_dev && bc_dev->defined() ? bc_dev->data_ptr<float>() : nullptr};
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)num_sms() * 8));
+  // Exactly the resident capacity (4 blocks of 256 per SM): every block streams an
+  // equal share in one wave, so no partial last wave idles most of the SMs.
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)num_sms() * 4));
   adamw_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<bf16*>(param.data_ptr()), master.data_ptr<float>(),
                                              m.data_ptr<float>(), v.data_ptr<float>(),
                                              reinterpret_cast<bf16*>(grad.data_ptr()), n, factor.data_ptr<float>(),

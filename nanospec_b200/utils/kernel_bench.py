@@ -79,9 +79,26 @@ def bench_adamw(a):
     m32, mm, vv = (torch.zeros(n, device="cuda") for _ in range(3))
     f = torch.ones(1, device="cuda")
     n2 = torch.ones(1, device="cuda")
-    us = _time(lambda: C.adamw_update(p, m32, mm, vv, g, f, n2, 1e-5, 0.01, 0.9, 0.999, 1e-8, 0.1, 0.03, 1.0),
-               a.reps, a.warmup)
-    return {"op": "adamw", "n": n, "us": round(us, 1), "TBps": round(26.0 * n / us / 1e6, 3)}
+    zero = not a.lazy
+    us = _time(lambda: C.adamw_update(p, m32, mm, vv, g, f, n2, 1e-5, 0.01, 0.9, 0.999, 1e-8, 0.1, 0.03, 1.0,
+                                      None, zero), a.reps, a.warmup)
+    # reads grad 2 + master/m/v 12; writes master/m/v 12 + param 2 (+ zeroed grad 2)
+    per = 30.0 if zero else 28.0
+    tbps = per * n / us / 1e6
+    return {"op": "adamw", "n": n, "zero_grad": zero, "bytes_per_param": per, "us": round(us, 1),
+            "TBps": round(tbps, 3), "of_measured_hbm": _of_peak(tbps * 1000)}
+
+
+def _of_peak(gbps):
+    """Fraction of the measured HBM copy bandwidth (MEASURED_PEAKS.json at the repo root)."""
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return round(gbps / float(json.load(f)["hbm_gbs"]), 3)
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def bench_head(a):
@@ -99,9 +116,13 @@ def bench_head(a):
     w2 = (torch.randn(a.vocab, a.rank, device=dev) * 0.02).bfloat16()
     dw2 = torch.empty_like(w2)
     us = _time(lambda: head_loss(h, W, e, w2, prep, o, target_hidden=th, dw2_out=dw2), a.reps, a.warmup)
-    flops = 2.0 * t * a.vocab * (2 * (a.hidden + a.rank) + a.hidden + a.hidden + 2 * a.rank)
+    # forward: draft logits (H) + Markov logits (r) + teacher logits (H); backward:
+    # dh (H), de (r), dW2 (r). Large T (chunked) also recomputes both logits blocks.
+    flops = 2.0 * t * a.vocab * (3 * a.hidden + 3 * a.rank)
+    reads = 2 * W.numel() * 2  # the LM head streams once per pass
     return {"op": "ce_kl_head", "tokens": t, "vocab": a.vocab, "us": round(us, 1),
-            "tflops": round(flops / us / 1e6, 1), "lm_head_reads_TBps": round(2 * W.numel() * 2 / us / 1e6, 3)}
+            "tflops": round(flops / us / 1e6, 1), "lm_head_reads_TBps": round(reads / us / 1e6, 3),
+            "of_measured_hbm": _of_peak(reads / us / 1e3)}
 
 
 def bench_attention(a):
@@ -141,7 +162,12 @@ def bench_gdn(a):
     g = -torch.rand(b, s, nv, device="cuda") * 0.1
     beta = torch.rand(b, s, nv, device="cuda").bfloat16()
     us = _time(lambda: vops.gated_delta_rule(q, k, v, g, beta, nv // nk), a.reps, a.warmup)
-    return {"op": "gdn_chunk_fwd", "S": s, "heads": nv, "us": round(us, 1)}
+    dout = torch.randn(b, s, nv, d, device="cuda").bfloat16()
+    bus = _time(lambda: vops.gated_delta_rule_backward(q, k, v, g, beta, dout, nv // nk), a.reps, a.warmup)
+    # chunked form, chunk 64: per head about 4*S*64*d (intra-chunk) + 4*S*d*d (state) MACs forward
+    flops = 2.0 * nv * (4 * s * 64 * d + 4 * s * d * d)
+    return {"op": "gdn_chunk", "S": s, "heads": nv, "fwd_us": round(us, 1), "bwd_us": round(bus, 1),
+            "fwd_tflops": round(flops / us / 1e6, 2)}
 
 
 def _graph_time(fns, reps):
@@ -228,6 +254,7 @@ def main(argv=None):
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--rotate", action="store_true", help="rotate operands through > L2 bytes")
+    p.add_argument("--lazy", action="store_true", help="adamw: leave the gradient in place (lazy_zero)")
     a = p.parse_args(argv)
     fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
           "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite}[a.op]
