@@ -17,10 +17,11 @@
 //             run in fp32.
 //   backward: dq  - the same decomposition (P recomputed from lse); it also stores
 //                   delta = rowsum(dO * O) for the dkv kernel;
-//             dkv - one CTA per (key tile, KV head, batch row): 16-key context tiles
-//                   and one tile per draft block. It walks the query blocks (and the
-//                   GQA heads) that see the tile and accumulates dK, dV in registers
-//                   in a fixed order: deterministic, no atomics.
+//             dkv - one CTA per (key tile, KV head, batch row): one tile per draft
+//                   block, and 16-key context tiles split further by GQA head (each
+//                   head's CTA writes fp32 partials, summed in head order). A CTA
+//                   walks the query blocks that see its tile and accumulates dK, dV
+//                   in registers in a fixed order: deterministic, no atomics.
 #include "common.h"
 #include "sm100.cuh"
 
@@ -35,6 +36,7 @@ struct AttnArgs {
   const bool* keep;                 // [b, nb]
   float* lse;                       // [b, Hq, Td]
   float* delta;                     // [b, Hq, Td] rowsum(dO * O), written by dq, read by dkv
+  float* part;                      // [2][G][b*S][Hk][D] fp32 per-head dK / dV of the context keys
   bf16 *out, *dq, *dk, *dv;
   int64_t lddk, lddv;
   int b, S, nb, bs, Hq, Hk;
@@ -43,7 +45,7 @@ struct AttnArgs {
 
 constexpr int NT = 128;    // threads of the forward / dq CTAs
 constexpr int KT = 64;     // keys per tile (forward / dq)
-constexpr int RMAX = 32;   // query rows per CTA (block_size)
+constexpr int RMAX = 32;   // largest block_size (query rows per CTA); kernels take RM in {8, 16, 32}
 
 __device__ __forceinline__ int64_t key_row(const AttnArgs& a, int bi, int kv) {
   // kv in [0, S) context, [S, S+Td) draft
@@ -125,22 +127,22 @@ __device__ __forceinline__ int64_t qoff(const AttnArgs& a, int bi, int j, int u,
 }
 
 // ---------------------------------------------------------------------------- forward
-template <int D>
+template <int D, int RM>
 __global__ void __launch_bounds__(NT) attn_fwd_kernel(AttnArgs a) {
   constexpr int KP = D + 2;
   constexpr int NP = D / 2;                       // column pairs
   constexpr int NG = NT / NP > 0 ? NT / NP : 1;   // row groups in the P V phase
-  constexpr int RPT = (RMAX + NG - 1) / NG;       // rows per thread in the P V phase
+  constexpr int RPT = (RM + NG - 1) / NG;       // rows per thread in the P V phase
   constexpr int SG = NT / KT;                     // row groups in the score phase
-  constexpr int RS = RMAX / SG;                   // rows per thread in the score phase
+  constexpr int RS = RM / SG;                   // rows per thread in the score phase
   extern __shared__ __align__(16) uint8_t dyn[];
   bf16* Ks = reinterpret_cast<bf16*>(dyn);             // [KT][KP]
   bf16* Vs = Ks + KT * KP;                             // [KT][KP]
-  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RMAX][D] q * scale
-  float* Ps = Qs + RMAX * D;                           // [RMAX][KT]
-  float* mrow = Ps + RMAX * KT;
-  float* lrow = mrow + RMAX;
-  float* corr = lrow + RMAX;
+  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RM][D] q * scale
+  float* Ps = Qs + RM * D;                           // [RM][KT]
+  float* mrow = Ps + RM * KT;
+  float* lrow = mrow + RM;
+  float* corr = lrow + RM;
   const int j = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
   const int hk = h / (a.Hq / a.Hk);
   const int R = a.bs, Td = a.nb * a.bs;
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(AttnArgs a) {
       Qs[r * D + d8 + 2 * t + 1] = f.y * a.scale;
     }
   }
-  if (tid < RMAX) {
+  if (tid < RM) {
     mrow[tid] = -INFINITY;
     lrow[tid] = 0.f;
   }
@@ -277,22 +279,22 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------- backward dq
-template <int D>
+template <int D, int RM>
 __global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(AttnArgs a) {
   constexpr int KP = D + 2;
   constexpr int NP = D / 2;
   constexpr int NG = NT / NP > 0 ? NT / NP : 1;
-  constexpr int RPT = (RMAX + NG - 1) / NG;
+  constexpr int RPT = (RM + NG - 1) / NG;
   constexpr int SG = NT / KT;
-  constexpr int RS = RMAX / SG;
+  constexpr int RS = RM / SG;
   extern __shared__ __align__(16) uint8_t dyn[];
   bf16* Ks = reinterpret_cast<bf16*>(dyn);             // [KT][KP]
   bf16* Vs = Ks + KT * KP;                             // [KT][KP]
-  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RMAX][D] q * scale
-  float* Os = Qs + RMAX * D;                           // [RMAX][D] dO
-  float* Ps = Os + RMAX * D;                           // [RMAX][KT] dS
-  float* lse_s = Ps + RMAX * KT;
-  float* delta_s = lse_s + RMAX;
+  float* Qs = reinterpret_cast<float*>(Vs + KT * KP);  // [RM][D] q * scale
+  float* Os = Qs + RM * D;                           // [RM][D] dO
+  float* Ps = Os + RM * D;                           // [RM][KT] dS
+  float* lse_s = Ps + RM * KT;
+  float* delta_s = lse_s + RM;
   const int j = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
   const int hk = h / (a.Hq / a.Hk);
   const int R = a.bs, Td = a.nb * a.bs;
@@ -414,27 +416,33 @@ __global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(AttnArgs a) {
 constexpr int NTK = 256;   // threads of the dkv CTAs
 constexpr int GRMAX = 64;  // G * block_size rows per query block
 
-template <int D, int TK, bool DRAFT>
+// GSPLIT: one CTA per (tile, KV head, GQA head g): rows of head g only, fp32 partial
+// dK/dV to a.part[g] (summed over g in order by attn_dkv_gsum_kernel). More CTAs for
+// the context tiles, which every query block sees.
+template <int D, int TK, bool DRAFT, bool GSPLIT>
 __global__ void __launch_bounds__(NTK) attn_bwd_dkv_kernel(AttnArgs a) {
+  constexpr int GRM = GSPLIT ? RMAX : GRMAX;  // rows per query block in this CTA
   constexpr int KP = D + 2;
   constexpr int NP = D / 2;
   constexpr int KG = NTK / NP > 0 ? NTK / NP : 1;  // key groups in the accumulation phase
   constexpr int KPT = (TK + KG - 1) / KG;          // keys per thread there
   constexpr int SG = NTK / TK;                     // row groups in the score phase
-  constexpr int RS = (GRMAX + SG - 1) / SG;        // rows per thread there
+  constexpr int RS = (GRM + SG - 1) / SG;          // rows per thread there
   extern __shared__ __align__(16) uint8_t dyn[];
   bf16* Ks = reinterpret_cast<bf16*>(dyn);
   bf16* Vs = Ks + TK * KP;
-  float* Qs = reinterpret_cast<float*>(Vs + TK * KP);  // [GRMAX][D] q (unscaled)
-  float* Os = Qs + GRMAX * D;                          // [GRMAX][D] dO
-  float* Ps = Os + GRMAX * D;                          // [GRMAX][TK]
-  float* DSs = Ps + GRMAX * TK;                        // [GRMAX][TK]
-  float* lse_s = DSs + GRMAX * TK;                     // [GRMAX]
-  float* delta_s = lse_s + GRMAX;                      // [GRMAX]
-  const int tile = blockIdx.x, hk = blockIdx.y, bi = blockIdx.z;
+  float* Qs = reinterpret_cast<float*>(Vs + TK * KP);  // [GRM][D] q (unscaled)
+  float* Os = Qs + GRM * D;                            // [GRM][D] dO
+  float* Ps = Os + GRM * D;                            // [GRM][TK]
+  float* DSs = Ps + GRM * TK;                          // [GRM][TK]
+  float* lse_s = DSs + GRM * TK;                       // [GRM]
+  float* delta_s = lse_s + GRM;                        // [GRM]
   const int G = a.Hq / a.Hk;
+  const int tile = blockIdx.x, bi = blockIdx.z;
+  const int hk = GSPLIT ? blockIdx.y / G : blockIdx.y;
+  const int g0 = GSPLIT ? blockIdx.y % G : 0;  // first GQA head of this CTA's rows
   const int Td = a.nb * a.bs;
-  const int GR = G * a.bs;
+  const int GR = (GSPLIT ? 1 : G) * a.bs;
   const int tid = threadIdx.x;
   int k0, cnt, jlo, jhi;
   if (!DRAFT) {
@@ -469,7 +477,7 @@ __global__ void __launch_bounds__(NTK) attn_bwd_dkv_kernel(AttnArgs a) {
     return j;
   };
   constexpr int C = D / 8;
-  constexpr int RIT = (GRMAX * C + NTK - 1) / NTK;
+  constexpr int RIT = (GRM * C + NTK - 1) / NTK;
   uint4 qr[RIT], orr[RIT];
   float lse_r = 0.f, delta_r = 0.f;
   auto fetch_rows = [&](int j) {
@@ -478,13 +486,13 @@ __global__ void __launch_bounds__(NTK) attn_bwd_dkv_kernel(AttnArgs a) {
       const int c = tid + i * NTK;
       if (c < GR * C) {
         const int gr = c / C, d8 = (c % C) * 8;
-        const int64_t off = qoff(a, bi, j, gr % a.bs, hk * G + gr / a.bs, D) + d8;
+        const int64_t off = qoff(a, bi, j, gr % a.bs, hk * G + g0 + gr / a.bs, D) + d8;
         qr[i] = *reinterpret_cast<const uint4*>(a.q + off);
         orr[i] = *reinterpret_cast<const uint4*>(a.dout + off);
       }
     }
     if (tid < GR) {
-      const int64_t ri = ((int64_t)bi * a.Hq + hk * G + tid / a.bs) * Td + j * a.bs + tid % a.bs;
+      const int64_t ri = ((int64_t)bi * a.Hq + hk * G + g0 + tid / a.bs) * Td + j * a.bs + tid % a.bs;
       lse_r = a.lse[ri];
       delta_r = a.delta[ri];
     }
@@ -571,12 +579,43 @@ __global__ void __launch_bounds__(NTK) attn_bwd_dkv_kernel(AttnArgs a) {
       const int kk = kg + KG * i;
       if (kk < cnt) {
         const int64_t row = key_row(a, bi, k0 + kk);
-        *reinterpret_cast<__nv_bfloat162*>(a.dk + row * a.lddk + hk * D + 2 * dp) =
-            __floats2bfloat162_rn(dK[i][0], dK[i][1]);
-        *reinterpret_cast<__nv_bfloat162*>(a.dv + row * a.lddv + hk * D + 2 * dp) =
-            __floats2bfloat162_rn(dV[i][0], dV[i][1]);
+        if (GSPLIT) {  // context keys only: row < b * S
+          const int64_t half = (int64_t)G * a.b * a.S * a.Hk * D;
+          const int64_t o = ((g0 * (int64_t)a.b * a.S + row) * a.Hk + hk) * D + 2 * dp;
+          *reinterpret_cast<float2*>(a.part + o) = make_float2(dK[i][0], dK[i][1]);
+          *reinterpret_cast<float2*>(a.part + half + o) = make_float2(dV[i][0], dV[i][1]);
+        } else {
+          *reinterpret_cast<__nv_bfloat162*>(a.dk + row * a.lddk + hk * D + 2 * dp) =
+              __floats2bfloat162_rn(dK[i][0], dK[i][1]);
+          *reinterpret_cast<__nv_bfloat162*>(a.dv + row * a.lddv + hk * D + 2 * dp) =
+              __floats2bfloat162_rn(dV[i][0], dV[i][1]);
+        }
       }
     }
+  }
+}
+
+// dK, dV of the context keys = sum over the G heads' fp32 partials, in head order.
+template <int D>
+__global__ void attn_dkv_gsum_kernel(AttnArgs a) {
+  const int G = a.Hq / a.Hk;
+  const int64_t pairs = (int64_t)a.b * a.S * a.Hk * (D / 2);
+  const int64_t half = (int64_t)G * a.b * a.S * a.Hk * D;
+  const int64_t stride_g = (int64_t)a.b * a.S * a.Hk * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < pairs; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = 2 * i;  // element of [b*S][Hk][D]
+    const int64_t row = e / (a.Hk * D), rem = e % (a.Hk * D);
+    float2 k2 = make_float2(0.f, 0.f), v2 = make_float2(0.f, 0.f);
+    for (int g = 0; g < G; ++g) {
+      const float2 pk = *reinterpret_cast<const float2*>(a.part + g * stride_g + e);
+      const float2 pv = *reinterpret_cast<const float2*>(a.part + half + g * stride_g + e);
+      k2.x += pk.x;
+      k2.y += pk.y;
+      v2.x += pv.x;
+      v2.y += pv.y;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(a.dk + row * a.lddk + rem) = __floats2bfloat162_rn(k2.x, k2.y);
+    *reinterpret_cast<__nv_bfloat162*>(a.dv + row * a.lddv + rem) = __floats2bfloat162_rn(v2.x, v2.y);
   }
 }
 
@@ -615,40 +654,71 @@ static AttnArgs make_args(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor a
   return a;
 }
 
-template <int D>
-static void fwd_d(AttnArgs a) {
+template <int D, int RM>
+static void fwd_rm(const AttnArgs& a) {
   constexpr int KP = D + 2;
-  const int smem = 2 * KT * KP * 2 + (RMAX * D + RMAX * KT + 3 * RMAX) * 4;
-  NS_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int smem = 2 * KT * KP * 2 + (RM * D + RM * KT + 3 * RM) * 4;
+  NS_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<D, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid(a.nb, a.Hq, a.b);
-  attn_fwd_kernel<D><<<grid, NT, smem, stream()>>>(a);
+  attn_fwd_kernel<D, RM><<<grid, NT, smem, stream()>>>(a);
   NS_CUDA(cudaGetLastError());
 }
 
-template <int D, int TK, bool DRAFT>
+// Row capacity = the smallest of 8 / 16 / 32 that holds a block (fewer registers
+// and less shared memory for the usual block_size 7).
+template <int D>
+static void fwd_d(AttnArgs a) {
+  if (a.bs <= 8) fwd_rm<D, 8>(a);
+  else if (a.bs <= 16) fwd_rm<D, 16>(a);
+  else fwd_rm<D, 32>(a);
+}
+
+template <int D, int RM>
+static void dq_rm(const AttnArgs& a) {
+  constexpr int KP = D + 2;
+  const int smem = 2 * KT * KP * 2 + (2 * RM * D + RM * KT + 2 * RM) * 4;
+  NS_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<D, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(a.nb, a.Hq, a.b);
+  attn_bwd_dq_kernel<D, RM><<<grid, NT, smem, stream()>>>(a);
+  NS_CUDA(cudaGetLastError());
+}
+
+template <int D, int TK, bool DRAFT, bool GSPLIT>
 static void dkv_launch(const AttnArgs& a, int tiles) {
   constexpr int KP = D + 2;
-  const int smem = 2 * TK * KP * 2 + (2 * GRMAX * D + 2 * GRMAX * TK + 2 * GRMAX) * 4;
-  auto kern = attn_bwd_dkv_kernel<D, TK, DRAFT>;
+  constexpr int GRM = GSPLIT ? RMAX : GRMAX;
+  const int smem = 2 * TK * KP * 2 + (2 * GRM * D + 2 * GRM * TK + 2 * GRM) * 4;
+  auto kern = attn_bwd_dkv_kernel<D, TK, DRAFT, GSPLIT>;
   NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  dim3 grid(tiles, a.Hk, a.b);
+  dim3 grid(tiles, GSPLIT ? a.Hk * (a.Hq / a.Hk) : a.Hk, a.b);
   kern<<<grid, NTK, smem, stream()>>>(a);
   NS_CUDA(cudaGetLastError());
 }
 
 template <int D>
 static void bwd_d(AttnArgs a) {
-  {
-    constexpr int KP = D + 2;
-    const int smem = 2 * KT * KP * 2 + (2 * RMAX * D + RMAX * KT + 2 * RMAX) * 4;
-    NS_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid(a.nb, a.Hq, a.b);
-    attn_bwd_dq_kernel<D><<<grid, NT, smem, stream()>>>(a);
-    NS_CUDA(cudaGetLastError());
-  }
+  if (a.bs <= 8) dq_rm<D, 8>(a);
+  else if (a.bs <= 16) dq_rm<D, 16>(a);
+  else dq_rm<D, 32>(a);
   constexpr int TKC = 16;
-  if (a.S > 0) dkv_launch<D, TKC, false>(a, (a.S + TKC - 1) / TKC);
-  dkv_launch<D, RMAX, true>(a, a.nb);
+  const int G = a.Hq / a.Hk;
+  at::Tensor part;
+  if (a.S > 0) {
+    const int tiles = (a.S + TKC - 1) / TKC;
+    if (G > 1) {
+      // context keys: one CTA per GQA head, then an ordered sum over the heads
+      part = at::empty({(int64_t)2 * G * a.b * a.S * a.Hk * D}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA));
+      a.part = part.data_ptr<float>();
+      dkv_launch<D, TKC, false, true>(a, tiles);
+      const int64_t pairs = (int64_t)a.b * a.S * a.Hk * (D / 2);
+      const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((pairs + 255) / 256, (int64_t)num_sms() * 4));
+      attn_dkv_gsum_kernel<D><<<blocks, 256, 0, stream()>>>(a);
+      NS_CUDA(cudaGetLastError());
+    } else {
+      dkv_launch<D, TKC, false, false>(a, tiles);
+    }
+  }
+  dkv_launch<D, RMAX, true, false>(a, a.nb);
 }
 
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,

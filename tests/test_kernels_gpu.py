@@ -190,9 +190,10 @@ def _attn_case(b=2, S=40, nb=4, bs=7, hq=10, hk=2, d=128):
 
 
 @cuda
-@pytest.mark.parametrize("d,hq,hk,S", [(128, 10, 2, 40), (128, 40, 8, 130), (32, 4, 2, 70)])
-def test_attention(d, hq, hk, S):
-    q, k, v, anchors, keep, S, bs = _attn_case(hq=hq, hk=hk, d=d, S=S)
+@pytest.mark.parametrize("d,hq,hk,S,bs", [(128, 10, 2, 40, 7), (128, 40, 8, 130, 7), (32, 4, 2, 70, 7),
+                                         (64, 4, 2, 70, 12), (32, 2, 2, 50, 20)])  # row capacities 8 / 16 / 32
+def test_attention(d, hq, hk, S, bs):
+    q, k, v, anchors, keep, S, bs = _attn_case(hq=hq, hk=hk, d=d, S=S, bs=bs)
     out, lse = ops.attention(q, k, v, anchors, keep, S, bs)
     qc, kc, vc = q.cpu().float(), k.cpu().float(), v.cpu().float()
     rout, rlse = ops.attention(qc, kc, vc, anchors.cpu(), keep.cpu(), S, bs)
