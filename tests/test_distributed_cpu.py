@@ -125,7 +125,7 @@ def _shard_layout(rank, world):
     assert all(torch.equal(exported[k], full[k]) for k in full)
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_shard_layout_and_export(world):
     run_ranks(world, _shard_layout)
 
