@@ -11,7 +11,8 @@ teacher tensors instead of a verifier), ``--comm {peer,nccl}``, ``--backend gloo
 Each step: every rank calls ``train(ids, model, objective, verifier=teacher,
 optimizer=opt)``; training ranks pool (numerator, denominator, accept sums) and
 rank 0 prints one JSON row ``{step, loss, accept_len, grad_norm, updated,
-denominator, seconds, ms_device}``. At the end the trainers save a checkpoint
+denominator, seconds, ms_device, phase_ms}`` (``phase_ms``: time per step phase, max
+over the training ranks). At the end the trainers save a checkpoint
 (same layout as the reference) and rank 0 writes the JSON report.
 """
 
@@ -29,6 +30,7 @@ import torch.distributed as dist
 
 from . import checkpoint
 from .config import TARGET_MODEL, TARGET_REVISION, DraftConfig, Objective, Topology, config_path
+from .utils.phases import PhaseTimer
 from .engine import TrainResult, train
 from .models.draft import DSpark, initialize
 from .parallel.node import Node, TeacherBatch
@@ -150,15 +152,16 @@ def main(argv=None):
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
         torch.manual_seed(args.seed + step * node.train_gpus + node.rank)
+        timer = PhaseTimer(node.device)
         if teacher is not None:
-            result = train(ids, model, o, verifier=teacher, optimizer=opt)
+            result = train(ids, model, o, verifier=teacher, optimizer=opt, phases=timer)
         elif node.training:
             g = torch.Generator(device=node.device).manual_seed(args.seed + 7 * step + node.rank)
             s = args.seq_len
             tb = TeacherBatch([torch.randn(1, s, c.hidden_size, device=node.device, generator=g).to(dtype)
                                for _ in c.target_layer_ids],
                               torch.randn(1, s, c.hidden_size, device=node.device, generator=g).to(dtype))
-            result = train(ids[node.rank:node.rank + 1], model, o, teacher_batch=tb, optimizer=opt)
+            result = train(ids[node.rank:node.rank + 1], model, o, teacher_batch=tb, optimizer=opt, phases=timer)
         else:
             result = None
         if node.training:
@@ -172,6 +175,14 @@ def main(argv=None):
                 ev1.record()
                 torch.cuda.synchronize()
                 row["ms_device"] = ev0.elapsed_time(ev1)
+            # device ms per phase, max over the training ranks (the slowest rank sets the pace)
+            phase = timer.summary()
+            names = ("verifier", "draft_forward", "head", "draft_backward", "optimizer")
+            pm = torch.tensor([phase.get(n, 0.0) for n in names], dtype=torch.float64,
+                              device=node.device if node.train_gpus > 1 else "cpu")
+            if node.train_gpus > 1:
+                dist.all_reduce(pm, op=dist.ReduceOp.MAX, group=node.train_group)
+            row["phase_ms"] = {n: round(float(v), 3) for n, v in zip(names, pm.tolist()) if n in phase}
             row["seconds"] = time.perf_counter() - t0
             rows.append(row)
             if node.rank == 0:

@@ -109,7 +109,7 @@ class DraftStep:
 
     @torch.no_grad()
     def run(self, ids, teacher: TeacherBatch, loss_mask, anchors, accumulation_steps, overlap,
-            resident=None):
+            resident=None, timer=None):
         m, o = self.model, self.o
         c = m.config
         dtype = m.dtype
@@ -195,6 +195,8 @@ class DraftStep:
             x = x_next
             sched.release(visit)
 
+        if timer is not None:
+            timer.mark("draft_forward")
         # ---------------------------------------------------------- head (fwd + bwd)
         visit = 1 + nl
         unit = sched.acquire(visit)
@@ -229,6 +231,8 @@ class DraftStep:
         _reduce(sched, visit, unit)
         del dh, de, e
 
+        if timer is not None:
+            timer.mark("head")
         # ---------------------------------------------------------- layers, reversed
         dc = torch.zeros(b * s, c.hidden_size, device=x.device, dtype=dtype)
         for j, layer in enumerate(reversed(m.layers)):
@@ -299,6 +303,8 @@ class DraftStep:
                                       inv.reshape(b * s, 1), norm.weight, g[f"fc_norm.{i}.weight"])
         _reduce(sched, visit, unit)
         sched.finish()
+        if timer is not None:
+            timer.mark("draft_backward")
         return metrics, hidden.view(b, td, -1)
 
 
@@ -315,7 +321,7 @@ def _split_kv(t, b, s, td):
 
 @torch.no_grad()
 def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=None, loss_mask=None,
-          optimizer=None, anchors=None, accumulation_steps=1, overlap=True, resident=None):
+          optimizer=None, anchors=None, accumulation_steps=1, overlap=True, resident=None, phases=None):
     """One synchronous step. See the module docstring.
 
     ``verifier``: a ``parallel.node.Teacher``; every rank of the node calls
@@ -324,12 +330,16 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
     ``optimizer``: an ``AdamW``; omit it to inspect raw gradients.
     ``overlap``: False selects the serial sharding schedule.
     ``resident``: keep gathered weights from forward to backward (default on CUDA, N>1).
+    ``phases``: a ``utils.phases.PhaseTimer``; the step marks verifier, draft_forward,
+    head, draft_backward and optimizer boundaries on it.
     """
     if verifier is not None and teacher_batch is not None:
         raise ValueError("Supply a verifier or fixed teacher tensors, not both")
     if verifier is not None:
         from .parallel.handoff import run_verifier
         teacher_batch, ids = run_verifier(ids, verifier)
+        if phases is not None:
+            phases.mark("verifier")
     if drafter is None:
         return TrainResult(teacher=teacher_batch)
     if teacher_batch is None or objective is None:
@@ -339,9 +349,11 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
         step = DraftStep(drafter, objective)
         drafter._draft_step = step
     metrics, hidden = step.run(ids, teacher_batch, loss_mask, anchors, accumulation_steps, overlap,
-                               resident)
+                               resident, timer=phases)
     update = None
     if optimizer is not None:
         from .parallel.optim import adamw_step
         update = adamw_step(optimizer, metrics.denominator, accumulation_steps, fused_norm=step.norm)
+        if phases is not None:
+            phases.mark("optimizer")
     return TrainResult(teacher_batch, metrics, hidden, update)

@@ -222,3 +222,6 @@ def test_cli_without_verifier_single_process():
         rows = main(["--config", "tiny", "--steps", "2", "--seq-len", "48", "--anchors", "4", "--dtype", "float32",
                      "--output", os.path.join(d, "r.json"), "--no-verifier", "--backend", "gloo"])
         assert len(rows) == 2
+        for r in rows:  # per-phase timing of every step
+            assert set(r["phase_ms"]) == {"draft_forward", "head", "draft_backward", "optimizer"}
+            assert all(v >= 0 for v in r["phase_ms"].values())
