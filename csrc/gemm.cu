@@ -25,6 +25,7 @@
 #include <cstdio>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "common.h"
 #include "gemm.h"
@@ -905,7 +906,24 @@ static int solo_smem(int bn, int kpb, bool cluster) {
   return std::max(used, std::min(min_smem, smem_max));
 }
 
+static GemmPlan plan_gemm_uncached(int M, int N, int K, int force_splits, bool amn, bool bmn);
+
+// Plans are pure functions of the problem; a training step reuses a fixed set of
+// shapes, so each is planned once per process (the search costs tens of microseconds
+// of host time, which matters for eagerly launched multi-rank steps).
 static GemmPlan plan_gemm(int M, int N, int K, int force_splits, bool amn = false, bool bmn = false) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, bool, bool>, GemmPlan> cache;
+  const auto key = std::make_tuple(M, N, K, force_splits, amn, bmn);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  const GemmPlan p = plan_gemm_uncached(M, N, K, force_splits, amn, bmn);
+  cache.emplace(key, p);
+  return p;
+}
+
+static GemmPlan plan_gemm_uncached(int M, int N, int K, int force_splits, bool amn, bool bmn) {
   const int sms = num_sms();
   auto base = [&](int bn) {
     GemmPlan p{};
