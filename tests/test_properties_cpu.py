@@ -7,7 +7,6 @@ nanospec/ops.py:48-66 and 129-162). These CPU statements are also the oracles th
 GPU kernel tests compare against.
 """
 
-import pytest
 import torch
 from hypothesis import HealthCheck, given, settings
 from hypothesis import strategies as st
@@ -94,3 +93,23 @@ def test_draft_attention_matches_reference(reference, b, s, nb, bs, groups, hk, 
     torch.testing.assert_close(dk[b * s:].reshape(b, td, hk, d), rk[:, s:], rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(dv[:b * s].reshape(b, s, hk, d), rv[:, :s], rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(dv[b * s:].reshape(b, td, hk, d), rv[:, s:], rtol=1e-4, atol=1e-5)
+
+
+@SETTINGS
+@given(b=st.integers(1, 2), s=st.integers(1, 70), h=st.integers(1, 3), dk=st.sampled_from([4, 8]),
+       dv=st.sampled_from([4, 8]), chunk=st.sampled_from([4, 16, 64]), seed=st.integers(0, 10_000))
+def test_gated_delta_rule_forms_agree(reference, b, s, h, dk, dv, chunk, seed):
+    # Our chunked (WY) form, our token-by-token oracle and the reference's chunked
+    # implementation (nanospec/ops.py:203-239) give the same outputs.
+    from nanospec_b200.ops import reference as ref
+    g_ = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, s, h, dk, generator=g_)
+    k = torch.randn(b, s, h, dk, generator=g_)
+    v = torch.randn(b, s, h, dv, generator=g_)
+    g = -torch.rand(b, s, h, generator=g_) * 0.5
+    beta = torch.rand(b, s, h, generator=g_)
+    rec = ref.gated_delta_rule_recurrent(q, k, v, g, beta)
+    ours = ref.gated_delta_rule_chunked(q, k, v, g, beta, chunk)
+    theirs = reference.ops.chunk_delta_rule(q, k, v, g, beta, chunk_size=chunk)
+    torch.testing.assert_close(ours, rec, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(theirs.float(), rec, rtol=1e-4, atol=1e-5)
