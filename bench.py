@@ -202,10 +202,6 @@ def main():
         o = RObjective(num_anchors=args.anchors)
     if args.impl == "ours" and world > 1 and args.comm == "peer":
         model.sharding.enable_peer()
-    if args.impl == "ours":
-        # The optimizer returns its scalars as device tensors: no host sync inside a
-        # step, so the host queues step i+1 while the GPU finishes step i.
-        opt.sync = False
     ids, states, last, mask = synthetic_batch(c, args.seq_len, rank, args.seed, dev, dtype)
     batch = TB(states, last)
 

@@ -14,7 +14,7 @@ from hypothesis import strategies as st
 import nanospec_b200 as N
 from nanospec_b200 import ops
 
-SETTINGS = settings(max_examples=25, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+SETTINGS = settings(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
 
 
 @SETTINGS
