@@ -160,17 +160,28 @@ def build(impl, c, world, rank, dev, dtype, seed):
     return model, opt, train, TeacherBatch
 
 
-def count_our_launches(step_fn):
-    """Kernels of this repository's extension launched by one step (names in namespace ns::)."""
+def profile_step(step_fn):
+    """One profiled step (outside the timed region): (kernels of this repository's
+    extension launched, communication ms, exposed communication ms). Exposed
+    communication is the part of the communication kernels' and peer copies' union
+    not covered by compute (utils.trace)."""
     from torch.profiler import ProfilerActivity, profile
+
+    from nanospec_b200.utils.trace import kernel_events, overlap_summary
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step_fn()
         torch.cuda.synchronize()
-    n = 0
-    for e in prof.events():
-        if e.device_type == torch.autograd.DeviceType.CUDA and "ns::" in e.name:
-            n += 1
-    return n
+    n = sum(1 for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA and "ns::" in e.name)
+    try:
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "trace.json")
+            prof.export_chrome_trace(path)
+            with open(path) as f:
+                summary = overlap_summary(kernel_events(json.load(f)["traceEvents"]))
+        return n, summary["comm_us"] / 1000.0, summary["exposed_comm_us"] / 1000.0
+    except (OSError, ValueError, KeyError) as exc:  # the analysis is optional; the count is not
+        print(f"bench: trace analysis skipped ({exc})", file=sys.stderr)
+        return n, float("nan"), float("nan")
 
 
 def main():
@@ -281,10 +292,12 @@ def main():
                    "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4 + 8,
                    "ms_per_step": round(e2e_ms, 3), "wall_ms_per_step": round(wall_ms, 3)}
 
-        launches = None
+        launches = comm_ms = exposed_ms = None
         if args.impl == "ours" and not args.no_count:
-            per_step = count_our_launches(step)
+            per_step, comm, exposed = profile_step(step)
             launches = per_step * args.steps
+            comm_ms = max_over_ranks(comm, world, dev)
+            exposed_ms = max_over_ranks(exposed, world, dev)
     value = n * args.seq_len / (ms / 1000)
     if rank == 0:
         out = {
@@ -314,6 +327,8 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "gpu_launches": launches,
+            "comm_ms_per_step": None if comm_ms is None or comm_ms != comm_ms else round(comm_ms, 3),
+            "exposed_comm_ms_per_step": None if exposed_ms is None or exposed_ms != exposed_ms else round(exposed_ms, 3),
         }
         if args.impl == "reference":
             out["impl"] = "reference"

@@ -4,14 +4,17 @@ Reference method (experiments/overlap.py:150-178): classify kernels of one
 profiled step as communication or compute by name; for every communication kernel,
 the union of its intersections with compute kernels on *other* streams is the
 hidden part. Here the communication set also contains this project's peer kernels
-(``peer_allgather``, ``peer_reduce_avg``, ``peer_wait``), and the summary adds the
-*exposed* communication time: the part of the union of communication intervals not
-covered by any compute kernel.
+(``peer_allgather``, ``peer_reduce_avg``, ``local_reduce_avg``, ``peer_wait``) and
+the copy-engine transfers of the peer schedule (memcpy activity on any stream other
+than the compute stream, which is the stream with the most kernels). The summary
+adds the *exposed* communication time: the part of the union of communication
+intervals not covered by any compute kernel.
 """
 
 from __future__ import annotations
 
-COMM_MARKERS = ("nccl", "peer_allgather", "peer_reduce", "peer_wait", "peer_signal")
+COMM_MARKERS = ("nccl", "peer_allgather", "peer_reduce", "local_reduce_avg", "peer_wait", "peer_signal")
+MEMCPY = "memcpy:"  # name prefix of copy-engine activity in kernel_events
 
 
 def _union(spans):
@@ -45,12 +48,15 @@ def _intersect(a, b):
 
 
 def kernel_events(trace_events):
-    """(name, start_us, end_us, stream) of the GPU kernels in a Chrome trace event list."""
+    """(name, start_us, end_us, stream) of the GPU kernels and memcpys in a Chrome trace
+    event list; memcpy names carry the ``memcpy:`` prefix."""
     out = []
     for e in trace_events:
-        if e.get("cat") == "kernel" and "dur" in e:
-            out.append((e.get("name", ""), float(e["ts"]), float(e["ts"]) + float(e["dur"]),
-                        e.get("args", {}).get("stream")))
+        cat = e.get("cat")
+        if cat in ("kernel", "gpu_memcpy") and "dur" in e:
+            name = e.get("name", "")
+            out.append(((MEMCPY + name) if cat == "gpu_memcpy" else name, float(e["ts"]),
+                        float(e["ts"]) + float(e["dur"]), e.get("args", {}).get("stream")))
     return out
 
 
@@ -61,8 +67,17 @@ def is_comm(name: str) -> bool:
 
 def overlap_summary(kernels):
     """Per-communication-kernel hidden time plus totals (microseconds)."""
-    comm = [k for k in kernels if is_comm(k[0])]
-    compute = [k for k in kernels if not is_comm(k[0])]
+    counts = {}
+    for k in kernels:
+        if not k[0].startswith(MEMCPY):
+            counts[k[3]] = counts.get(k[3], 0) + 1
+    main = max(counts, key=counts.get) if counts else None
+
+    def comm_like(k):
+        return is_comm(k[0]) or (k[0].startswith(MEMCPY) and k[3] != main)
+
+    comm = [k for k in kernels if comm_like(k)]
+    compute = [k for k in kernels if not comm_like(k)]
     rows = []
     for name, lo, hi, stream in comm:
         spans = _union([(max(lo, c[1]), min(hi, c[2])) for c in compute
