@@ -153,3 +153,19 @@ def test_fused_grad_norm_matches_separate_pass():
     for s in m.sharding:
         cuda_ops().grad_norm_sq(s.grad, f, b)
     assert abs(a.item() - b.item()) <= 1e-5 * b.item(), (a.item(), b.item())
+
+
+@cuda
+def test_phase_timer_on_device():
+    from nanospec_b200.utils.phases import PhaseTimer
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    m = _model(c, "cuda", torch.bfloat16)
+    ids = torch.randint(0, c.vocab_size, (1, 128), device="cuda")
+    hs = [torch.randn(1, 128, c.hidden_size, device="cuda").bfloat16() for _ in range(2)]
+    last = torch.randn(1, 128, c.hidden_size, device="cuda").bfloat16()
+    timer = PhaseTimer("cuda")
+    N.train(ids, m, N.Objective(num_anchors=8), teacher_batch=N.TeacherBatch(hs, last),
+            optimizer=N.AdamW(m.sharding, lr=1e-3), phases=timer)
+    ph = timer.summary()
+    assert set(ph) == {"draft_forward", "head", "draft_backward", "optimizer"}
+    assert all(v > 0 for v in ph.values())
