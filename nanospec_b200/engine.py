@@ -2,7 +2,8 @@
 
 Public API (reference: nanospec/train.py:22-401):
 ``train(ids, drafter, objective, *, verifier=, teacher_batch=, loss_mask=,
-optimizer=, anchors=, accumulation_steps=1, overlap=True) -> TrainResult``.
+optimizer=, anchors=, accumulation_steps=1, overlap=True, resident=None, phases=None)
+-> TrainResult``.
 
 Execution differs from the reference in layout, not in math:
 
@@ -14,13 +15,15 @@ Execution differs from the reference in layout, not in math:
 * residual adds ride in GEMM epilogues; RoPE is fused with the per-head RMSNorm;
 * the head (LM head + Markov head + CE/KL) runs forward and backward back to back
   (``objective.head_loss``), so the heads unit is visited once per step;
-* the context-projection input gradient is only formed when ``fc_norm`` needs it.
+* the context-projection input gradient is only formed when ``fc_norm`` needs it;
+* with one rank and gradients written in place, the weight-gradient GEMMs also
+  produce the optimizer's gradient norm (``parallel.optim.FusedGradNorm``);
+* ``phases=`` marks device-timed phase boundaries (``utils.phases``).
 """
 
 from __future__ import annotations
 
 import os
-
 from dataclasses import dataclass
 
 import torch
