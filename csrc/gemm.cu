@@ -17,9 +17,13 @@
 //              residual / accumulate.
 // K depth per stage: 128 for small-N tiles (weight-streaming products, where the
 // per-stage handshake between producer, MMA issuer and barrier dominates), 64 for
-// wide tiles. Split-K: every split writes an fp32 partial; the last CTA of a tile to
-// finish (per-tile arrival counter) sums the partials in split order 0..S-1 and
-// runs the epilogue, so results are deterministic and no second kernel is launched.
+// wide tiles. Split-K (up to 8 splits): the splits of a tile form a thread-block
+// cluster; each parks its fp32 partial in its own shared memory and, after a cluster
+// barrier, reduces 1/S of the tile over DSMEM in split order 0..S-1. More splits use
+// fp32 partials in global memory and a last-arriving-CTA fix-up (per-tile arrival
+// counter). Either way the result is deterministic and no second kernel runs.
+// Grids with more tiles than SMs use gemm_bf16_persistent (below). plan_gemm picks
+// tile width, split count and kernel from a time model, once per problem shape.
 // Every mbarrier wait is bounded; a timeout sets the device error flag.
 #include <cmath>
 #include <cstdio>
