@@ -63,6 +63,8 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, 
                                       at::Tensor dout, int64_t groups);
 int64_t device_error();
 void clear_device_error();
+at::Tensor device_error_tensor();
+void reset_device_error_state();
 }  // namespace ns
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -114,4 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
   m.def("clear_device_error", &ns::clear_device_error);
+  m.def("device_error_tensor", &ns::device_error_tensor, "the error word as a 1-element int32 CUDA view");
+  m.def("reset_device_error_state", &ns::reset_device_error_state,
+        "after a timed-out wait: clear split-K counters and the error word");
 }

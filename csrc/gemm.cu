@@ -730,11 +730,8 @@ static void launch_persistent_bn(const CUtensorMap& ta, const CUtensorMap& tb, c
                                  const GemmArgs& a, int mt, int units) {
   using P = PersistCfg<BN>;
   auto kern = gemm_bf16_persistent<BN, AMN, BMN>;
-  static bool attr = false;
-  if (!attr) {
-    NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  once_per_device(attr, [&] { NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM)); });
   const int grid = std::min(units, num_sms());
   kern<<<grid, 192, P::SMEM, stream()>>>(ta, tb, to, a, mt, units);
   NS_CUDA(cudaGetLastError());
@@ -755,11 +752,10 @@ template <int BN, bool AMN, bool BMN>
 static void launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, int stages) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, AMN, BMN>;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<unsigned long long> attr{0};
+  once_per_device(attr, [&] {
     NS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_MAX));
-    attr = true;
-  }
+  });
   // TMEM holds 512 columns per SM: reserve enough shared memory that no more than
   // k = 512 / TMEM_COLS CTAs co-reside (an allocation never has to wait), i.e. k+1
   // CTAs (each also pays 1 KB of reserved shared memory) must not fit in 228 KB.
@@ -814,9 +810,14 @@ static int max_stages(int bn, bool solo) {
   }
 }
 
-// Per-(device, stream) arrival counters for split-K; each launch leaves them zero.
+// Per-(device, stream) arrival counters for split-K; each launch leaves them zero,
+// unless a CTA gave up on a bounded wait (then `gemm_reset_counters` clears them).
+static std::mutex g_counter_mu;
+static std::map<std::pair<int, cudaStream_t>, std::pair<unsigned*, int>> g_counter_pool;
+
 static unsigned* split_counters(int tiles) {
-  static std::map<std::pair<int, cudaStream_t>, std::pair<unsigned*, int>> pool;
+  std::lock_guard<std::mutex> lock(g_counter_mu);
+  auto& pool = g_counter_pool;
   int dev;
   NS_CUDA(cudaGetDevice(&dev));
   auto key = std::make_pair(dev, stream());
@@ -830,6 +831,17 @@ static unsigned* split_counters(int tiles) {
     return p;
   }
   return it->second.first;
+}
+
+// Zeroes every split-K arrival counter array of the current device (all streams).
+// Called after a bounded wait timed out; waits for the device first.
+void gemm_reset_counters() {
+  int dev;
+  NS_CUDA(cudaGetDevice(&dev));
+  NS_CUDA(cudaDeviceSynchronize());
+  std::lock_guard<std::mutex> lock(g_counter_mu);
+  for (auto& kv : g_counter_pool)
+    if (kv.first.first == dev) NS_CUDA(cudaMemset(kv.second.first, 0, kv.second.second * sizeof(unsigned)));
 }
 
 static long long* g_trace = nullptr;  // test hook (gemm_trace)
@@ -1175,7 +1187,8 @@ static_assert(kNoallocPartialsOff + 4ull * NSB_GEMM_NOALLOC_PARTIAL_FLOATS <= NS
 
 constexpr int kNoallocMaxDevices = 64;
 static std::mutex g_noalloc_mu;
-static unsigned char* g_noalloc_base[kNoallocMaxDevices] = {nullptr};
+// Written once per device under g_noalloc_mu (release); read without the lock (acquire).
+static std::atomic<unsigned char*> g_noalloc_base[kNoallocMaxDevices] = {};
 static thread_local char g_noalloc_msg[256] = "";
 
 static int noalloc_fail(int code, const char* what, cudaError_t e = cudaSuccess) {
@@ -1203,14 +1216,14 @@ static cudaError_t noalloc_set_attr_bn() {
 // the kernels' shared-memory limit.
 static int noalloc_setup_current(int dev) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_base[dev]) return 0;
+  if (g_noalloc_base[dev].load(std::memory_order_acquire)) return 0;
   void* p = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
   if (e != cudaSuccess) return noalloc_fail(3, "cudaGetSymbolAddress(scratch)", e);
   if ((e = noalloc_set_attr_bn<64>()) != cudaSuccess || (e = noalloc_set_attr_bn<128>()) != cudaSuccess ||
       (e = noalloc_set_attr_bn<192>()) != cudaSuccess || (e = noalloc_set_attr_bn<256>()) != cudaSuccess)
     return noalloc_fail(3, "cudaFuncSetAttribute", e);
-  g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+  g_noalloc_base[dev].store(static_cast<unsigned char*>(p), std::memory_order_release);
   return 0;
 }
 
@@ -1272,11 +1285,12 @@ extern "C" int nsb_gemm_bf16_splitk_noalloc(const void* a, int a_mn_major, long 
   if ((a_mn_major ? a_rows != K || a_cols != M : a_rows != M || a_cols != K) ||
       (b_mn_major ? b_rows != K || b_cols != N : b_rows != N || b_cols != K))
     return noalloc_fail(1, "operand shapes do not match M, N, K and their majors");
+  if (a_ld < a_cols || b_ld < b_cols) return noalloc_fail(1, "row stride smaller than row length");
   if (out_ld < N || (reinterpret_cast<uintptr_t>(out) % 16) != 0)
     return noalloc_fail(1, "out must be 16-byte aligned with a row stride >= N");
   int dev = 0;
   if (int rc = noalloc_current(&dev)) return rc;
-  if (!g_noalloc_base[dev])
+  if (!g_noalloc_base[dev].load(std::memory_order_acquire))
     if (int rc = noalloc_setup_current(dev)) return rc;
 
   const int bn = pick_bn(N);
@@ -1286,7 +1300,7 @@ extern "C" int nsb_gemm_bf16_splitk_noalloc(const void* a, int a_mn_major, long 
   const int tiles = mt * nt;
   const int kpb = (kb + splits - 1) / splits;
   const int eff_splits = (kb + kpb - 1) / kpb;  // same split plan as the torch path
-  if ((unsigned)tiles > NSB_GEMM_NOALLOC_MAX_TILES) {
+  if (eff_splits > 1 && (unsigned)tiles > NSB_GEMM_NOALLOC_MAX_TILES) {  // only split launches use counters
     std::snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%d output tiles exceed the maximum of %u", tiles,
                   NSB_GEMM_NOALLOC_MAX_TILES);
     return 2;
@@ -1309,7 +1323,7 @@ extern "C" int nsb_gemm_bf16_splitk_noalloc(const void* a, int a_mn_major, long 
   const bool solo = (long long)tiles * eff_splits <= sms;
   const int stages = std::max(1, std::min(max_stages(bn, solo), kpb));
 
-  unsigned char* base = g_noalloc_base[dev];
+  unsigned char* base = g_noalloc_base[dev].load(std::memory_order_acquire);
   GemmArgs ga{};
   ga.M = M;
   ga.N = N;
@@ -1341,9 +1355,9 @@ extern "C" int nsb_gemm_noalloc_status(int* status) {
   if (!status) return noalloc_fail(1, "null status pointer");
   int dev = 0;
   if (int rc = noalloc_current(&dev)) return rc;
-  if (!g_noalloc_base[dev])
+  if (!g_noalloc_base[dev].load(std::memory_order_acquire))
     if (int rc = noalloc_setup_current(dev)) return rc;
-  cudaError_t e = cudaMemcpy(status, g_noalloc_base[dev] + kNoallocStatusOff, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaError_t e = cudaMemcpy(status, g_noalloc_base[dev].load(std::memory_order_acquire) + kNoallocStatusOff, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return noalloc_fail(3, "cudaMemcpy(status)", e);
   return 0;
 }
@@ -1353,9 +1367,9 @@ extern "C" int nsb_gemm_noalloc_reset(void* stream) {
   g_noalloc_msg[0] = 0;
   int dev = 0;
   if (int rc = noalloc_current(&dev)) return rc;
-  if (!g_noalloc_base[dev])
+  if (!g_noalloc_base[dev].load(std::memory_order_acquire))
     if (int rc = noalloc_setup_current(dev)) return rc;
-  cudaError_t e = cudaMemsetAsync(g_noalloc_base[dev], 0, kNoallocPartialsOff, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaMemsetAsync(g_noalloc_base[dev].load(std::memory_order_acquire), 0, kNoallocPartialsOff, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return noalloc_fail(3, "cudaMemsetAsync(counters)", e);
   return 0;
 }

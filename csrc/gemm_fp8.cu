@@ -251,11 +251,10 @@ void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = out.stride(0);
   a.err = device_error_flag();
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<unsigned long long> attr{0};
+  once_per_device(attr, [&] {
     NS_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM));
-    attr = true;
-  }
+  });
   dim3 grid((unsigned)((T + F8_BM - 1) / F8_BM), (unsigned)(N / F8_BN));
   fp8_gemm_kernel<<<grid, 192, F8_SMEM, stream()>>>(ta, tb, a);
   NS_CUDA(cudaGetLastError());

@@ -9,6 +9,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <atomic>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -70,6 +71,19 @@ inline int num_sms() {
     NS_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
   }
   return n;
+}
+
+// Runs `set` once per device: function attributes (cudaFuncSetAttribute) belong to
+// one device's context, so a process that launches on several devices sets them on
+// each. `mask` is a per-call-site bit set indexed by device ordinal.
+template <class F>
+inline void once_per_device(std::atomic<unsigned long long>& mask, F&& set) {
+  int dev;
+  NS_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (mask.load(std::memory_order_acquire) & bit) return;
+  set();
+  mask.fetch_or(bit, std::memory_order_acq_rel);
 }
 
 // Device-side error word shared by the kernels' bounded waits: a kernel whose

@@ -18,12 +18,15 @@
 // Operands: `a` is A with rows x cols elements and row stride a_ld; a_mn_major = 0
 // means A is [M, K] (K-major), 1 means A is stored [K, M] (MN-major). The same for
 // `b` with N in place of M. All three pointers 16-byte aligned; the strides of A and
-// B a multiple of 8 elements (TMA rules); out_ld >= N.
+// B a multiple of 8 elements (TMA rules) and at least their row lengths
+// (a_ld >= a_cols, b_ld >= b_cols); out_ld >= N.
 //
 // Limits: splits in [1, 16]; splits * M * N * 4 bytes of partials must fit in the
-// partial area (NSB_GEMM_NOALLOC_PARTIAL_FLOATS floats); at most
-// NSB_GEMM_NOALLOC_MAX_TILES output tiles (128 x BN, BN = 64..256 by N). Larger
-// problems are rejected with an error code and a message; they are not truncated.
+// partial area (NSB_GEMM_NOALLOC_PARTIAL_FLOATS floats); a launch that splits K
+// (more than one effective split) has at most NSB_GEMM_NOALLOC_MAX_TILES output
+// tiles (128 x BN, BN = 64..256 by N), one arrival counter each. An unsplit launch
+// uses no scratch and has no tile limit. Larger problems are rejected with an
+// error code and a message; they are not truncated.
 //
 // State that must start at zero: the per-tile arrival counters. Static device
 // storage starts zeroed and every completed launch leaves the counters it used at

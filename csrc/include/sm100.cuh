@@ -81,6 +81,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (no tensor map), completing
+// on `bar` with `bytes` of transaction count. Both addresses 16-byte aligned and
+// `bytes` a multiple of 16. Source must be this GPU's own memory.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Tiled TMA store of a box from this CTA's shared memory (bulk-group completion).
 // Rows / columns outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {

@@ -1,6 +1,7 @@
 // Frozen-verifier kernels (forward only): (1+w)-RMSNorm, gated RMSNorm, residual add,
-// SiLU*up, causal depthwise conv + SiLU, GDN gates, the chunked gated delta rule, and
-// causal GQA attention with partial RoPE and a sigmoid output gate.
+// SiLU*up, causal depthwise conv + SiLU, GDN gates, and causal GQA attention with
+// partial RoPE and a sigmoid output gate. The chunked gated delta rule is in
+// gdn_fwd.cu.
 //
 // Casting follows the plain PyTorch statements of the same ops (compute dtype bf16,
 // fp32 inside reductions), so results agree with the CPU path to bf16 resolution.
@@ -111,160 +112,6 @@ __global__ void gdn_gates_kernel(const bf16* __restrict__ a, const bf16* __restr
     g[i] = -expf(alog[h]) * sp;
     const float bv = bf(b[i]);
     beta[i] = __float2bfloat16(1.f / (1.f + expf(-bv)));
-  }
-}
-
-// ------------------------------------------------------------------ chunked gated delta rule
-// One CTA per (batch row, value head); chunks of 64 tokens in sequence; state S [D][D]
-// fp32 in shared memory. Value head h reads key head h / groups.
-// Per chunk (cumulative in-chunk decay G):
-//   T = (I + tril(beta_i k_i.k_j e^{G_i - G_j}, -1))^-1            forward substitution
-//   W = T (beta k e^G) ;  U = T (beta v)
-//   v' = U - W S ;  o = (q e^G) S + tril(q k^T e^{G_i-G_j}) v'
-//   S = e^{G_last} S + (k e^{G_last - G})^T v'
-template <int D>
-__global__ void __launch_bounds__(256) gdn_chunk_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                            const bf16* __restrict__ v, const float* __restrict__ gin,
-                                                            const bf16* __restrict__ beta_in, bf16* __restrict__ out,
-                                                            int s, int nk, int nv, int groups) {
-  constexpr int C = 64;
-  extern __shared__ float sm[];
-  float* S = sm;                 // [D][D]
-  float* Tm = S + D * D;         // [C][C]
-  float* Wb = Tm + C * C;        // [C][D]
-  float* Ub = Wb + C * D;        // [C][D]
-  bf16* qs = reinterpret_cast<bf16*>(Ub + C * D);  // [C][D] normalised q (bf16)
-  bf16* ks = qs + C * D;                           // [C][D] normalised k
-  bf16* vs = ks + C * D;                           // [C][D]
-  __shared__ float G[C], Bt[C];
-  const int h = blockIdx.x, bi = blockIdx.y;
-  const int hk = h / groups;
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
-  const float qscale = rsqrtf((float)D);
-  for (int i = tid; i < D * D; i += nt) S[i] = 0.f;
-  const int nchunks = (s + C - 1) / C;
-  for (int ch = 0; ch < nchunks; ++ch) {
-    const int t0 = ch * C;
-    const int cnt = min(C, s - t0);
-    __syncthreads();
-    // load + L2-normalise q, k (bf16 statement: rsqrt(sum(x*x) + 1e-6) rounded), v raw
-    for (int r = warp; r < C; r += nw) {
-      const bool in = r < cnt;
-      const int64_t tq = ((int64_t)bi * s + t0 + r);
-      float sq = 0.f, sk = 0.f;
-      for (int d = lane; d < D; d += 32) {
-        const float a = in ? bf(q[(tq * nk + hk) * D + d]) : 0.f;
-        const float b = in ? bf(k[(tq * nk + hk) * D + d]) : 0.f;
-        sq += rb(a * a);
-        sk += rb(b * b);
-      }
-      sq = warp_sum(sq);
-      sk = warp_sum(sk);
-      const float iq = rb(rsqrtf(rb(rb(sq) + 1e-6f)));
-      const float ik = rb(rsqrtf(rb(rb(sk) + 1e-6f)));
-      for (int d = lane; d < D; d += 32) {
-        const float a = in ? bf(q[(tq * nk + hk) * D + d]) : 0.f;
-        const float b = in ? bf(k[(tq * nk + hk) * D + d]) : 0.f;
-        qs[r * D + d] = __float2bfloat16(a * iq);
-        ks[r * D + d] = __float2bfloat16(b * ik);
-        vs[r * D + d] = in ? v[(tq * nv + h) * D + d] : __float2bfloat16(0.f);
-      }
-      if (lane == 0) {
-        G[r] = in ? gin[tq * nv + h] : 0.f;
-        Bt[r] = in ? bf(beta_in[tq * nv + h]) : 0.f;
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float acc = 0.f;
-      for (int r = 0; r < C; ++r) {
-        acc += G[r];
-        G[r] = acc;
-      }
-    }
-    __syncthreads();
-    // M (strictly lower) into Tm, A = tril(q k^T Gamma) into Wb? (kept separate below)
-    for (int idx = tid; idx < C * C; idx += nt) {
-      const int i = idx / C, j = idx % C;
-      float m = 0.f;
-      if (j < i) {
-        float dot = 0.f;
-        for (int d = 0; d < D; ++d) dot += bf(ks[i * D + d]) * bf(ks[j * D + d]);
-        m = Bt[i] * dot * expf(G[i] - G[j]);
-      }
-      Tm[idx] = m;
-    }
-    __syncthreads();
-    // In-place inverse of the unit lower-triangular (I + M): row i of T =
-    // e_i - sum_{j<i} M_ij T_j (rows j < i already final). Column c handled by thread c.
-    for (int i = 1; i < C; ++i) {
-      float val = 0.f;
-      if (tid < C) {
-        const int c = tid;
-        if (c < i) {
-          float acc = -Tm[i * C + c];  // j = c term with T_cc = 1
-          for (int j = c + 1; j < i; ++j) acc -= Tm[i * C + j] * Tm[j * C + c];
-          val = acc;
-        }
-      }
-      __syncthreads();
-      if (tid < C && tid < i) Tm[i * C + tid] = val;
-      __syncthreads();
-    }
-    // W = T (beta k e^G), U = T (beta v), including the unit diagonal.
-    for (int idx = tid; idx < C * D; idx += nt) {
-      const int i = idx / D, d = idx % D;
-      float w = Bt[i] * bf(ks[i * D + d]) * expf(G[i]);
-      float u = Bt[i] * bf(vs[i * D + d]);
-      for (int j = 0; j < i; ++j) {
-        const float t = Tm[i * C + j];
-        w += t * Bt[j] * bf(ks[j * D + d]) * expf(G[j]);
-        u += t * Bt[j] * bf(vs[j * D + d]);
-      }
-      Wb[idx] = w;
-      Ub[idx] = u;
-    }
-    __syncthreads();
-    // v' = U - W S  (into Ub)
-    for (int idx = tid; idx < C * D; idx += nt) {
-      const int i = idx / D, e = idx % D;
-      float acc = 0.f;
-      for (int d = 0; d < D; ++d) acc += Wb[i * D + d] * S[d * D + e];
-      Ub[idx] -= acc;
-    }
-    __syncthreads();
-    // attention-like intra-chunk term A = tril(q k^T Gamma) into Tm (T no longer needed)
-    for (int idx = tid; idx < C * C; idx += nt) {
-      const int i = idx / C, j = idx % C;
-      float a = 0.f;
-      if (j <= i) {
-        float dot = 0.f;
-        for (int d = 0; d < D; ++d) dot += bf(qs[i * D + d]) * bf(ks[j * D + d]);
-        a = dot * qscale * expf(G[i] - G[j]);
-      }
-      Tm[idx] = a;
-    }
-    __syncthreads();
-    // o = (q e^G) S + A v'
-    for (int idx = tid; idx < C * D; idx += nt) {
-      const int i = idx / D, e = idx % D;
-      if (i >= cnt) continue;
-      float acc = 0.f;
-      for (int d = 0; d < D; ++d) acc += bf(qs[i * D + d]) * S[d * D + e];
-      acc *= qscale * expf(G[i]);
-      for (int j = 0; j <= i; ++j) acc += Tm[i * C + j] * Ub[j * D + e];
-      out[(((int64_t)bi * s + t0 + i) * nv + h) * D + e] = __float2bfloat16(acc);
-    }
-    __syncthreads();
-    // S = e^{G_last} S + (k e^{G_last - G})^T v'
-    const float gl = G[C - 1];
-    for (int idx = tid; idx < D * D; idx += nt) {
-      const int d = idx / D, e = idx % D;
-      float acc = S[idx] * expf(gl);
-      for (int j = 0; j < C; ++j) acc += bf(ks[j * D + d]) * expf(gl - G[j]) * Ub[j * D + e];
-      S[idx] = acc;
-    }
   }
 }
 
@@ -413,29 +260,6 @@ void gdn_gates(at::Tensor a, at::Tensor b, at::Tensor alog, at::Tensor dtb, at::
                                                           dtb.data_ptr<float>(), g.data_ptr<float>(), BP(beta), nv,
                                                           a.numel());
   NS_CUDA(cudaGetLastError());
-}
-
-template <int D>
-static void gdn_launch(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, int groups, at::Tensor out) {
-  const int b = q.size(0), s = q.size(1), nk = q.size(2), nv = v.size(2);
-  constexpr int C = 64;
-  const int smem = (D * D + C * C + 2 * C * D) * 4 + 3 * C * D * 2;
-  NS_CUDA(cudaFuncSetAttribute(gdn_chunk_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  gdn_chunk_fwd_kernel<D><<<dim3(nv, b), 256, smem, stream()>>>(CBP(q), CBP(k), CBP(v), g.data_ptr<float>(), CBP(beta),
-                                                               BP(out), s, nk, nv, groups);
-  NS_CUDA(cudaGetLastError());
-}
-
-void gdn_chunk_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, int64_t groups, at::Tensor out) {
-  NS_CHECK(q.size(3) == v.size(3), "gated delta rule kernel needs d_k == d_v");
-  NS_CHECK(g.scalar_type() == at::kFloat, "g must be fp32");
-  switch (q.size(3)) {
-    case 16: gdn_launch<16>(q, k, v, g, beta, groups, out); break;
-    case 32: gdn_launch<32>(q, k, v, g, beta, groups, out); break;
-    case 64: gdn_launch<64>(q, k, v, g, beta, groups, out); break;
-    case 128: gdn_launch<128>(q, k, v, g, beta, groups, out); break;
-    default: NS_CHECK(false, "gated delta rule head dim must be 16, 32, 64 or 128");
-  }
 }
 
 template <int D>

@@ -103,18 +103,31 @@ class Topology:
     ``world - N`` ranks own contiguous verifier layer ranges, in order. With
     ``colocate=True`` (1-GPU boxes, or when every GPU trains) the verifier runs
     on the training ranks themselves, partitioned over them.
+
+    ``replicate=True`` is the layout a 180 GB GPU makes possible: every training
+    rank holds the whole FP8 verifier (about 27 GB at the 27B shape) and runs it on
+    its own batch row, so there is no pipeline bubble and the hand-off is local.
+    The reference's layout (contiguous partitions over ``world - N`` inference
+    ranks, nanospec/distributed.py:41-63) remains the default of ``for_world``.
     """
 
     world: int
     train_gpus: int
     colocate: bool = False
     inference_ranks: list[int] = field(default_factory=list)
+    replicate: bool = False
 
     def __post_init__(self):
         if self.train_gpus not in (1, 2, 4, 8):
             raise ValueError("training ranks must be 1, 2, 4 or 8")
         if self.train_gpus > self.world:
             raise ValueError("more training ranks than GPUs")
+        if self.replicate:
+            if self.train_gpus != self.world:
+                raise ValueError("a replicated verifier needs every GPU to train")
+            self.colocate = True
+            self.inference_ranks = list(range(self.world))
+            return
         if not self.inference_ranks:
             if self.world == self.train_gpus:
                 self.colocate = True
@@ -128,6 +141,11 @@ class Topology:
         if train_gpus is None:
             train_gpus = {1: 1, 2: 1, 4: 2, 8: 4}.get(world, 1)
         return cls(world=world, train_gpus=train_gpus)
+
+    @classmethod
+    def replicated(cls, world: int) -> "Topology":
+        """Every GPU trains and holds a full verifier replica."""
+        return cls(world=world, train_gpus=world, replicate=True)
 
 
 def config_path(name: str) -> Path:

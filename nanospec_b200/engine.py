@@ -335,14 +335,24 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
     ``resident``: keep gathered weights from forward to backward (default on CUDA, N>1).
     ``phases``: a ``utils.phases.PhaseTimer``; the step marks verifier, draft_forward,
     head, draft_backward and optimizer boundaries on it.
+
+    On CUDA, the kernels' bounded-wait error word is snapshotted after each phase
+    without a host wait (``utils.health``); a wait that timed out raises
+    ``DeviceWaitTimeout`` at the end of this call (synchronous optimizer) or at the
+    start of the next one. ``NANOSPEC_DEVICE_CHECK=0`` turns the check off.
     """
     if verifier is not None and teacher_batch is not None:
         raise ValueError("Supply a verifier or fixed teacher tensors, not both")
+    health = _monitor(ids)
+    if health is not None:
+        health.check()  # a bounded wait of an earlier step that timed out raises here
     if verifier is not None:
         from .parallel.handoff import run_verifier
         teacher_batch, ids = run_verifier(ids, verifier)
         if phases is not None:
             phases.mark("verifier")
+        if health is not None:
+            health.snapshot("verifier")
     if drafter is None:
         return TrainResult(teacher=teacher_batch)
     if teacher_batch is None or objective is None:
@@ -353,10 +363,24 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
         drafter._draft_step = step
     metrics, hidden = step.run(ids, teacher_batch, loss_mask, anchors, accumulation_steps, overlap,
                                resident, timer=phases)
+    if health is not None:
+        health.snapshot("draft forward/backward")
     update = None
     if optimizer is not None:
         from .parallel.optim import adamw_step
         update = adamw_step(optimizer, metrics.denominator, accumulation_steps, fused_norm=step.norm)
         if phases is not None:
             phases.mark("optimizer")
+        if health is not None:
+            health.snapshot("optimizer")
+            # A synchronous optimizer has just waited for the device: the snapshots
+            # taken so far are complete, so a timeout in this step raises now.
+            health.check()
     return TrainResult(teacher_batch, metrics, hidden, update)
+
+
+def _monitor(ids):
+    if not (torch.is_tensor(ids) and ids.is_cuda) or os.environ.get("NANOSPEC_DEVICE_CHECK", "1") == "0":
+        return None
+    from .utils.health import monitor
+    return monitor(ids.device)

@@ -11,6 +11,9 @@ of the step); outputs are device tensors owned by the graph (``TrainResult`` wit
 tensors). Anchors are drawn inside the graph from the CUDA generator's graph-safe
 stream, so consecutive replays see fresh anchors.
 
+Each replay snapshots the kernels' bounded-wait error word (``utils.health``); a
+timeout raises ``DeviceWaitTimeout`` at the next ``step``.
+
 Restrictions: one training rank (the peer and NCCL schedules keep host-side
 sequence state and are not captured), fixed shapes, no verifier in the step.
 """
@@ -73,5 +76,17 @@ class GraphedStep:
             self.loss_mask.copy_(loss_mask, non_blocking=True)
         if logits is not None:
             self.logits.copy_(logits, non_blocking=True)
+        health = self._health()
+        if health is not None:
+            health.check()  # an earlier replay's bounded wait that timed out raises here
         self.graph.replay()
+        if health is not None:
+            health.snapshot("graphed training step")
         return self.result
+
+    def _health(self):
+        import os
+        if os.environ.get("NANOSPEC_DEVICE_CHECK", "1") == "0":
+            return None
+        from .utils.health import monitor
+        return monitor(self.ids.device)

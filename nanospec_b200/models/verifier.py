@@ -157,20 +157,23 @@ def quantize_weight_blocks(w: torch.Tensor, block=128):
 
 @torch.no_grad()
 def write_synthetic_checkpoint(path, text_config: dict, *, seed=0, fp8=True, std=0.02,
-                               shard_bytes=4 << 30, dtype=torch.bfloat16) -> Path:
-    """Random-init checkpoint in the HF Qwen3.5 FP8 layout (tensors generated on CPU).
+                               shard_bytes=4 << 30, dtype=torch.bfloat16, device="cpu") -> Path:
+    """Random-init checkpoint in the HF Qwen3.5 FP8 layout.
 
     ``fp8=False`` keeps projections in ``dtype`` (needed when widths are not multiples
     of 128). Norm weights are small random offsets (the (1+w) convention), A_log and
-    dt_bias follow the usual GDN initialisation ranges.
+    dt_bias follow the usual GDN initialisation ranges. ``device="cuda"`` draws and
+    quantizes the tensors on the GPU (a 27B-shaped checkpoint takes seconds instead
+    of many minutes); the files are the same format either way.
     """
     from safetensors.torch import save_file
     path = Path(path)
     path.mkdir(parents=True, exist_ok=True)
     tc = dict(text_config)
-    gen = torch.Generator().manual_seed(seed)
+    gen = torch.Generator(device=device).manual_seed(seed)
     h, v = tc["hidden_size"], tc["vocab_size"]
     shard, shard_size, files, weight_map = {}, 0, [], {}
+    rand = lambda shape: torch.randn(shape, generator=gen, device=device)  # noqa: E731
 
     def flush():
         nonlocal shard, shard_size
@@ -185,42 +188,36 @@ def write_synthetic_checkpoint(path, text_config: dict, *, seed=0, fp8=True, std
 
     def put(name, t):
         nonlocal shard_size
-        shard[name] = t.contiguous()
+        shard[name] = t.contiguous().cpu()
         shard_size += t.numel() * t.element_size()
         if shard_size >= shard_bytes:
             flush()
 
-    put(PREFIX + "embed_tokens.weight", (torch.randn(v, h, generator=gen) * std).to(dtype))
+    put(PREFIX + "embed_tokens.weight", (rand((v, h)) * std).to(dtype))
     for i in range(tc["num_hidden_layers"]):
         for name, (shape, quant) in layer_tensor_shapes(tc, i).items():
             full = PREFIX + name
             if name.endswith("A_log"):
-                put(full, torch.log(torch.empty(shape).uniform_(1, 16, generator=gen)).float())
+                put(full, torch.log(torch.empty(shape, device=device).uniform_(1, 16, generator=gen)).float())
             elif name.endswith("dt_bias"):
-                put(full, (torch.rand(shape, generator=gen) * 0.5).float())
+                put(full, (torch.rand(shape, generator=gen, device=device) * 0.5).float())
             elif name.endswith("conv1d.weight"):
-                put(full, (torch.randn(shape, generator=gen) * 0.3).to(dtype))
+                put(full, (rand(shape) * 0.3).to(dtype))
             elif len(shape) == 1:
-                put(full, (torch.randn(shape, generator=gen) * 0.05).to(dtype))
+                put(full, (rand(shape) * 0.05).to(dtype))
             else:
-                w = torch.randn(shape, generator=gen) * std
+                w = rand(shape) * std
                 if quant and fp8 and shape[0] % 128 == 0 and shape[1] % 128 == 0:
                     q, s = quantize_weight_blocks(w)
                     put(full + ".weight", q)
                     put(full + ".weight_scale_inv", s)
                 else:
                     put(full + ".weight", w.to(dtype))
-    put(PREFIX + "norm.weight", (torch.randn(h, generator=gen) * 0.05).to(dtype))
-    put("lm_head.weight", (torch.randn(v, h, generator=gen) * std).to(dtype))
+                del w
+    put(PREFIX + "norm.weight", (rand(h) * 0.05).to(dtype))
+    put("lm_head.weight", (rand((v, h)) * std).to(dtype))
     flush()
-    config = {
-        "model_type": "qwen3_5",
-        "architectures": ["Qwen3_5ForConditionalGeneration"],
-        "text_config": tc,
-        "quantization_config": {"quant_method": "fp8", "weight_block_size": [128, 128],
-                                "activation_scheme": "dynamic", "fmt": "e4m3"},
-        "synthetic": {"seed": seed, "fp8": fp8},
-    }
+    config = synthetic_hf_config(tc, seed=seed, fp8=fp8)
     (path / "config.json").write_text(json.dumps(config, indent=2))
     (path / "model.safetensors.index.json").write_text(
         json.dumps({"metadata": {}, "weight_map": weight_map}, indent=2))
@@ -301,11 +298,18 @@ class QwenDecoderLayer(nn.Module):
 
 
 class QwenStage(nn.Module):
-    """Contiguous layer range [start, end) of the verifier, with embed (first) / norm+head (last)."""
+    """Contiguous layer range [start, end) of the verifier, with embed (first) / norm+head (last).
 
-    def __init__(self, checkpoint: Checkpoint, start, end, *, device, first=False, last=False):
+    Weights come from ``checkpoint`` (HF layout, as the reference's ``QwenStage``,
+    nanospec/qwen.py:144-188) or, with ``checkpoint=None``, from ``weights`` (names
+    without the ``model.language_model.`` prefix) and ``config`` (a full HF
+    ``config.json`` dict), e.g. ``random_verifier_weights``.
+    """
+
+    def __init__(self, checkpoint: Checkpoint | None, start, end, *, device, first=False, last=False,
+                 weights: dict | None = None, config: dict | None = None):
         super().__init__()
-        cfg = checkpoint.config
+        cfg = checkpoint.config if checkpoint is not None else config
         tc = self.config = cfg["text_config"]
         if cfg.get("model_type") != "qwen3_5":
             raise ValueError("Only the dense Qwen3.5 text backbone is implemented")
@@ -315,19 +319,76 @@ class QwenStage(nn.Module):
         if tc["rope_parameters"].get("rope_type", "default") != "default":
             raise ValueError("Only default RoPE is supported")
         self.start, self.end = start, end
-        keys = [k for k in checkpoint.index
-                if any(k.startswith(f"{PREFIX}layers.{i}.") for i in range(start, end))]
-        if first:
-            keys.append(PREFIX + "embed_tokens.weight")
-        if last:
-            keys += [PREFIX + "norm.weight", "lm_head.weight"]
-        loaded = checkpoint.load(keys, device)
-        w = {(k[len(PREFIX):] if k.startswith(PREFIX) else k): v for k, v in loaded.items()}
+        if checkpoint is not None:
+            keys = [k for k in checkpoint.index
+                    if any(k.startswith(f"{PREFIX}layers.{i}.") for i in range(start, end))]
+            if first:
+                keys.append(PREFIX + "embed_tokens.weight")
+            if last:
+                keys += [PREFIX + "norm.weight", "lm_head.weight"]
+            loaded = checkpoint.load(keys, device)
+            w = {(k[len(PREFIX):] if k.startswith(PREFIX) else k): v for k, v in loaded.items()}
+        else:
+            w = weights
         self.layers = nn.ModuleList([QwenDecoderLayer(tc, w, i) for i in range(start, end)])
         self.embed_tokens = _W(w["embed_tokens.weight"]) if first else None
         self.norm = _W(w["norm.weight"], tc["rms_norm_eps"]) if last else None
         self.lm_head = _W(w["lm_head.weight"]) if last else None
         self.eval()
+
+
+def synthetic_hf_config(text_config: dict, *, seed=0, fp8=True) -> dict:
+    """The ``config.json`` dict of a synthetic Qwen3.5 FP8 checkpoint."""
+    return {
+        "model_type": "qwen3_5",
+        "architectures": ["Qwen3_5ForConditionalGeneration"],
+        "text_config": dict(text_config),
+        "quantization_config": {"quant_method": "fp8", "weight_block_size": [128, 128],
+                                "activation_scheme": "dynamic", "fmt": "e4m3"},
+        "synthetic": {"seed": seed, "fp8": fp8},
+    }
+
+
+@torch.no_grad()
+def random_verifier_weights(text_config: dict, start: int, end: int, *, device, first=False, last=False,
+                            seed=0, std=0.02, dtype=torch.bfloat16, embed=None, lm_head=None) -> dict:
+    """Random-init weights of layers [start, end) generated on ``device`` (no checkpoint).
+
+    Same value ranges as ``write_synthetic_checkpoint``; FP8 projections are
+    quantized per 128 x 128 block on the device. ``embed`` / ``lm_head``, when
+    given, are used instead of fresh tensors (so a draft and the verifier can share
+    the frozen target tensors).
+    """
+    tc = text_config
+    gen = torch.Generator(device=device).manual_seed(seed)
+    h, v = tc["hidden_size"], tc["vocab_size"]
+    out = {}
+    for i in range(start, end):
+        for name, (shape, quant) in layer_tensor_shapes(tc, i).items():
+            if name.endswith("A_log"):
+                out[name] = torch.log(torch.empty(shape, device=device).uniform_(1, 16, generator=gen))
+            elif name.endswith("dt_bias"):
+                out[name] = torch.rand(shape, device=device, generator=gen) * 0.5
+            elif name.endswith("conv1d.weight"):
+                out[name] = (torch.randn(shape, device=device, generator=gen) * 0.3).to(dtype)
+            elif len(shape) == 1:
+                out[name] = (torch.randn(shape, device=device, generator=gen) * 0.05).to(dtype)
+            else:
+                w = torch.randn(shape, device=device, generator=gen) * std
+                if quant and shape[0] % 128 == 0 and shape[1] % 128 == 0:
+                    q, sc = quantize_weight_blocks(w)
+                    out[name + ".weight"], out[name + ".weight_scale_inv"] = q, sc
+                else:
+                    out[name + ".weight"] = w.to(dtype)
+                del w
+    if first:
+        out["embed_tokens.weight"] = embed if embed is not None else \
+            (torch.randn(v, h, device=device, generator=gen) * std).to(dtype)
+    if last:
+        out["norm.weight"] = (torch.randn(h, device=device, generator=gen) * 0.05).to(dtype)
+        out["lm_head.weight"] = lm_head if lm_head is not None else \
+            (torch.randn(v, h, device=device, generator=gen) * std).to(dtype)
+    return out
 
 
 # ---------------------------------------------------------------------------- execution

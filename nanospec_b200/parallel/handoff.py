@@ -31,32 +31,72 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from ..models.verifier import Checkpoint, QwenStage, stage_forward
+from ..models.verifier import Checkpoint, QwenStage, random_verifier_weights, stage_forward, synthetic_hf_config
 from .node import TeacherBatch
 
 
 class Teacher(nn.Module):
-    """The verifier as seen from one rank: partition table plus this rank's stage."""
+    """The verifier as seen from one rank: partition table plus this rank's stage.
 
-    def __init__(self, node, path, capture, *, checkpoint=None):
+    With a replicated topology (``Topology.replicated``) every rank owns all layers
+    and runs them on its own batch row; otherwise partitions are contiguous layer
+    ranges over ``node.inference_ranks`` (reference: nanospec/distributed.py:41-63).
+    """
+
+    def __init__(self, node, path, capture, *, checkpoint=None, weights=None, config=None):
         super().__init__()
         self.node = node
-        self.checkpoint = checkpoint or Checkpoint(path)
-        self.config = self.checkpoint.text_config
+        if weights is None:
+            self.checkpoint = checkpoint or Checkpoint(path)
+            self.config = self.checkpoint.text_config
+        else:
+            self.checkpoint = None
+            self.config = config["text_config"]
         self.capture = tuple(capture)
         n = self.config["num_hidden_layers"]
         ranks = node.inference_ranks
-        self.partitions = {r: (i * n // len(ranks), (i + 1) * n // len(ranks)) for i, r in enumerate(ranks)}
+        self.replicated = bool(getattr(node.topology, "replicate", False))
+        if self.replicated:
+            self.partitions = {r: (0, n) for r in ranks}
+        else:
+            self.partitions = {r: (i * n // len(ranks), (i + 1) * n // len(ranks)) for i, r in enumerate(ranks)}
         self.stage = None
         world = dist.get_world_size() if dist.is_initialized() else 1
         # Collective: every rank constructs its Teacher, so every rank creates this group.
-        self.handoff_group = dist.new_group(list(range(world))) if world > 1 else None
+        self.handoff_group = dist.new_group(list(range(world))) if world > 1 and not self.replicated else None
         if node.rank in ranks:
             start, end = self.partitions[node.rank]
-            self.stage = QwenStage(self.checkpoint, start, end, device=node.device,
-                                   first=node.rank == ranks[0], last=node.rank == ranks[-1])
+            first = self.replicated or node.rank == ranks[0]
+            last = self.replicated or node.rank == ranks[-1]
+            self.stage = QwenStage(self.checkpoint, start, end, device=node.device, first=first, last=last,
+                                   weights=weights, config=config)
+
+    @classmethod
+    def random(cls, node, text_config, capture, *, seed=0, embed=None, lm_head=None):
+        """A verifier with random-init weights generated on this rank's device.
+
+        Only this rank's layers are drawn (all of them when replicated). ``embed`` /
+        ``lm_head`` let the verifier share the frozen target tensors with a draft.
+        """
+        n = text_config["num_hidden_layers"]
+        ranks = node.inference_ranks
+        weights = None
+        if node.rank in ranks:
+            if getattr(node.topology, "replicate", False):
+                start, end, first, last = 0, n, True, True
+            else:
+                i = ranks.index(node.rank)
+                start, end = i * n // len(ranks), (i + 1) * n // len(ranks)
+                first, last = i == 0, i == len(ranks) - 1
+            weights = random_verifier_weights(text_config, start, end, device=node.device, first=first,
+                                              last=last, seed=seed + start, embed=embed, lm_head=lm_head)
+        else:
+            weights = {}
+        return cls(node, None, capture, weights=weights, config=synthetic_hf_config(text_config, seed=seed))
 
     def owner(self, layer):
+        if self.replicated:
+            return self.node.rank
         return next(r for r, (a, b) in self.partitions.items() if a <= layer < b)
 
 
@@ -69,6 +109,11 @@ def run_verifier(ids, verifier: Teacher, microbatch_rows: int = 1):
     (and no logits), plus ``ids[r:r+1]``; other ranks get ``(None, ids)``.
     """
     node, stage = verifier.node, verifier.stage
+    if verifier.replicated:
+        # Every rank runs the whole verifier on its own row: the hand-off is local.
+        row = ids[node.rank:node.rank + 1] if ids.shape[0] > 1 else ids
+        out, captured = stage_forward(stage, row, capture=verifier.capture)
+        return TeacherBatch([captured[layer] for layer in verifier.capture], out, None), row
     ranks = node.inference_ranks
     b, s = ids.shape
     width = verifier.config["hidden_size"]

@@ -7,6 +7,12 @@
     python -m nanospec_b200.utils.kernel_bench fp8 --T 4096 --k 5120 --nout 17408
     python -m nanospec_b200.utils.kernel_bench gdn --S 4096 --heads 48
     python -m nanospec_b200.utils.kernel_bench gemm-suite
+    python -m nanospec_b200.utils.kernel_bench verifier --S 4096
+
+``verifier`` runs four random-init decoder layers of the Qwen3.5-27B shape (three
+gated-DeltaNet layers and one full-attention layer) on one row of S tokens and
+reports the device time of every verifier op, summed per op kind, plus the whole
+4-layer stage.
 
 ``gemm-suite`` times every linear product of one draft layer at the benchmark
 shape (forward, input and weight gradients; qwen draft: hidden 5120, FFN 15360,
@@ -170,6 +176,58 @@ def bench_gdn(a):
             "fwd_tflops": round(flops / us / 1e6, 2)}
 
 
+def bench_verifier(a):
+    from nanospec_b200.models.verifier import (QwenStage, qwen3_5_27b_text_config, random_verifier_weights,
+                                               stage_forward, synthetic_hf_config)
+    from nanospec_b200.ops import verifier_ops as vops
+    tc = qwen3_5_27b_text_config()
+    tc["num_hidden_layers"] = 4
+    tc["layer_types"] = tc["layer_types"][:4]
+    w = random_verifier_weights(tc, 0, 4, device="cuda", first=True, last=True, seed=0)
+    st = QwenStage(None, 0, 4, device="cuda", first=True, last=True, weights=w,
+                   config=synthetic_hf_config(tc))
+    ids = torch.randint(0, tc["vocab_size"], (1, a.S), device="cuda")
+    names = ("embedding", "add", "silu_mul", "qwen_norm", "qwen_gated_norm", "fp8_linear", "causal_conv_silu",
+             "gdn_gates", "gated_delta_rule", "causal_attention_gated")
+    times, orig = {}, {n: getattr(vops, n) for n in names}
+
+    def wrap(name, fn):
+        def run(*args, **kw):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(*args, **kw)
+            e1.record()
+            times.setdefault(name, []).append((e0, e1))
+            return out
+        return run
+    for _ in range(a.warmup):
+        stage_forward(st, ids)
+    torch.cuda.synchronize()
+    whole = _time(lambda: stage_forward(st, ids), a.reps, 0) / 1000.0
+    for n in names:
+        setattr(vops, n, wrap(n, orig[n]))
+    try:
+        for _ in range(a.reps):
+            stage_forward(st, ids)
+        torch.cuda.synchronize()
+    finally:
+        for n in names:
+            setattr(vops, n, orig[n])
+    per = {n: round(sum(e0.elapsed_time(e1) for e0, e1 in v) / a.reps, 3) for n, v in times.items()}
+    return {"op": "verifier_4_layers", "S": a.S, "stage_ms": round(whole, 3), "op_ms": per,
+            "fp8_tflops": round(_verifier_fp8_flops(tc, a.S) / (per.get("fp8_linear", 1e9) * 1e9), 1)}
+
+
+def _verifier_fp8_flops(tc, s):
+    from nanospec_b200.models.verifier import layer_tensor_shapes
+    total = 0.0
+    for i in range(tc["num_hidden_layers"]):
+        for (shape, quant) in layer_tensor_shapes(tc, i).values():
+            if quant and len(shape) == 2:
+                total += 2.0 * s * shape[0] * shape[1]
+    return total
+
+
 def _graph_time(fns, reps):
     """Per-call time of `fns` (one call each) captured in one CUDA graph and replayed."""
     s = torch.cuda.Stream()
@@ -239,7 +297,8 @@ def bench_gemm_suite(a):
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn", "gemm-suite"))
+    p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn", "gemm-suite",
+                                     "verifier"))
     p.add_argument("--kind", choices=("fwd", "dgrad", "wgrad"), default="fwd")
     p.add_argument("--T", type=int, default=56)
     p.add_argument("--nout", type=int, default=5120)
@@ -257,7 +316,8 @@ def main(argv=None):
     p.add_argument("--lazy", action="store_true", help="adamw: leave the gradient in place (lazy_zero)")
     a = p.parse_args(argv)
     fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
-          "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite}[a.op]
+          "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite,
+          "verifier": bench_verifier}[a.op]
     print(json.dumps(fn(a)), flush=True)
 
 

@@ -225,3 +225,46 @@ def test_cli_without_verifier_single_process():
         for r in rows:  # per-phase timing of every step
             assert set(r["phase_ms"]) == {"draft_forward", "head", "draft_backward", "optimizer"}
             assert all(v >= 0 for v in r["phase_ms"].values())
+
+
+# ---------------------------------------------------------------------------- replicated verifier
+def _replicated(rank, world, outdir):
+    import math
+
+    from nanospec_b200.config import Topology
+    from nanospec_b200.models.verifier import QwenStage, stage_forward, synthetic_hf_config, tiny_hybrid_text_config
+    from nanospec_b200.parallel.handoff import Teacher
+    tc = tiny_hybrid_text_config()
+    node = N.Node(world, topology=Topology.replicated(world), backend="gloo")
+    assert node.training and node.inference_ranks == list(range(world))
+    c = N.DraftConfig.load(N.config_path("tiny-hybrid"))
+    g = torch.Generator().manual_seed(5)
+    emb = (torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1).bfloat16()
+    head = (torch.randn(c.vocab_size, c.hidden_size, generator=g) * 0.1).bfloat16()
+    teacher = Teacher.random(node, tc, c.target_layer_ids, seed=11, embed=emb, lm_head=head)
+    assert teacher.stage.start == 0 and teacher.stage.end == 4 and teacher.handoff_group is None
+    # the verifier and the draft share the frozen target tensors
+    assert teacher.stage.embed_tokens.weight.data_ptr() == emb.data_ptr()
+    ids = torch.randint(0, c.vocab_size, (world, 48), generator=torch.Generator().manual_seed(3))
+    res = N.train(ids, verifier=teacher)
+    x, cap = stage_forward(teacher.stage, ids[rank:rank + 1], capture=c.target_layer_ids)
+    for got, layer in zip(res.teacher.hidden_states, c.target_layer_ids):
+        assert torch.equal(got, cap[layer])
+    assert torch.equal(res.teacher.last_hidden, x)
+    # every replica holds the same weights: one seed, one draw
+    w = teacher.stage.layers[0].mlp.gate_proj.weight.float().sum().reshape(1)
+    ws = [torch.zeros(1) for _ in range(world)]
+    dist.all_gather(ws, w)
+    assert all(torch.equal(ws[0], t) for t in ws)
+    model = N.DSpark(c, N.initialize(c, 1, torch.float32), emb, head, device="cpu", dtype=torch.float32,
+                     group=node.train_group, world_size=world, rank=rank)
+    opt = N.AdamW(model.sharding, lr=1e-3)
+    torch.manual_seed(rank)
+    r = N.train(ids, model, N.Objective(num_anchors=4, block_size=4), verifier=teacher, optimizer=opt)
+    assert r.update["updated"] and math.isfinite(float(r.metrics.loss))
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_replicated_verifier_topology(world):
+    with tempfile.TemporaryDirectory() as d:
+        run_ranks(world, _replicated, d)

@@ -160,3 +160,75 @@ def test_failed_rank_surfaces_as_error_not_hang():
     assert "injected failure" in reports[1][0]
     assert reports[0][0] != "finished", reports  # the surviving rank's collective failed
     assert reports[0][1] < 100
+
+
+# ---------------------------------------------------------------------------- device wait timeouts
+class _FlakyWord:
+    """A host error word that a 'kernel' sets during one phase of the step.
+
+    ``lag=True`` makes every snapshot look still in flight until ``land()`` is
+    called, like a device copy that the host has not waited for.
+    """
+
+    def __init__(self, phase, lag=False):
+        self.word = torch.zeros(1, dtype=torch.int32)
+        self.phase = phase
+        self.resets = 0
+        self.lag = lag
+        self.landed = not lag
+
+    def land(self):
+        self.landed = True
+
+    def monitor(self):
+        from nanospec_b200.utils.health import ErrorMonitor
+        mon = ErrorMonitor("cpu", word=self.word, reset=self._reset)
+        snap = mon.snapshot
+        flaky = self
+
+        class _Later:
+            def query(self):
+                return flaky.landed
+
+            def synchronize(self):
+                flaky.landed = True
+
+        def snapshot(tag):
+            if tag == self.phase:
+                self.word.fill_(2)  # a peer flag wait gave up during this phase
+            snap(tag)
+            if self.lag:
+                slot, _, t = mon.pending[-1]
+                mon.pending[-1] = (slot, _Later(), t)
+        mon.snapshot = snapshot
+        return mon
+
+    def _reset(self):
+        self.resets += 1
+        self.word.zero_()
+
+
+@pytest.mark.parametrize("lag", [False, True])
+def test_device_wait_timeout_raises_on_host(monkeypatch, lag):
+    """A bounded device wait that gave up (code in the error word) becomes a Python
+    exception naming the phase: in the same call when the snapshot has landed (a
+    synchronous optimizer waited), else at the start of the next call."""
+    from nanospec_b200 import engine
+    from nanospec_b200.utils.health import DeviceWaitTimeout
+    c, m = _model()
+    opt = N.AdamW(m.sharding, lr=1e-3)
+    flaky = _FlakyWord("draft forward/backward", lag=lag)
+    mon = flaky.monitor()
+    monkeypatch.setattr(engine, "_monitor", lambda ids: mon)
+    if not lag:
+        with pytest.raises(DeviceWaitTimeout, match="peer-memory flag wait.*draft forward/backward"):
+            _step(c, m, opt)
+    else:
+        _step(c, m, opt)  # the snapshots are still "in flight": no wait, no raise
+        flaky.land()
+        with pytest.raises(DeviceWaitTimeout, match="draft forward/backward"):
+            _step(c, m, opt)
+    assert flaky.resets == 1 and int(flaky.word) == 0
+    flaky.phase, flaky.lag, flaky.landed = None, False, True  # the next step is clean again
+    r = _step(c, m, opt)
+    assert bool(r.update["updated"])

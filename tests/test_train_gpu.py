@@ -169,3 +169,44 @@ def test_phase_timer_on_device():
     ph = timer.summary()
     assert set(ph) == {"draft_forward", "head", "draft_backward", "optimizer"}
     assert all(v > 0 for v in ph.values())
+
+
+@cuda
+def test_train_raises_when_a_device_wait_times_out():
+    """A bounded device wait that runs out inside a real train() step (here: a peer
+    flag wait on a flag that nothing sets, injected at the head phase) makes train()
+    raise DeviceWaitTimeout on the host instead of returning a silent step; the
+    device state is reset and the next step runs normally."""
+    from nanospec_b200.ops._ext import cuda_ops
+    from nanospec_b200.utils.health import DeviceWaitTimeout
+    from nanospec_b200.utils.phases import PhaseTimer
+    C = cuda_ops()
+    C.clear_device_error()
+    wid, _ = C.window_create(1 << 20, 0, 1)
+    C.window_open(wid, C.window_ipc_handle(wid).view(1, -1))
+
+    class Stuck(PhaseTimer):
+        def mark(self, name):
+            super().mark(name)
+            if name == "head":
+                C.peer_wait(wid, 0, 5, 1, 2000)  # gives up after ~0.4 ms of polling
+
+    c = N.DraftConfig.load(N.config_path("tiny"))
+    dev = torch.device("cuda")
+    m = _model(c, dev, torch.bfloat16)
+    opt = N.AdamW(m.sharding, lr=1e-3)
+    o = N.Objective(num_anchors=4)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, c.vocab_size, (1, 64), generator=g).cuda()
+    tb = N.TeacherBatch([torch.randn(1, 64, c.hidden_size, generator=g).bfloat16().cuda()
+                         for _ in range(c.num_target_layers)],
+                        torch.randn(1, 64, c.hidden_size, generator=g).bfloat16().cuda())
+    try:
+        with pytest.raises(DeviceWaitTimeout, match="peer-memory flag wait.*draft forward/backward"):
+            N.train(ids, m, o, teacher_batch=tb, optimizer=opt, phases=Stuck(dev))
+        assert C.device_error() == 0  # reset before raising
+        r = N.train(ids, m, o, teacher_batch=tb, optimizer=opt)
+        assert r.update["updated"]
+    finally:
+        torch.cuda.synchronize()
+        C.window_close(wid)

@@ -86,3 +86,63 @@ def test_noalloc_gemm_rejects_oversized_scratch():
     assert rc == 2
     assert b"scratch holds at most" in lib.nsb_gemm_noalloc_error()
     assert _call(lib, a, False, b, False, out, M, N, K, 17) == 1
+
+
+def _raw(lib, ptr, a_mn, a_rows, a_cols, a_ld, b_mn, b_rows, b_cols, b_ld, out_ptr, out_ld, M, N, K, splits):
+    stream = torch.cuda.current_stream().cuda_stream
+    return lib.nsb_gemm_bf16_splitk_noalloc(ptr, a_mn, a_rows, a_cols, a_ld, ptr, b_mn, b_rows, b_cols, b_ld,
+                                            out_ptr, out_ld, M, N, K, splits, stream)
+
+
+@cuda
+def test_noalloc_gemm_argument_checks_launch_nothing():
+    """Arguments the entry point must refuse before it builds a tensor map or
+    launches: these calls only pass sizes (the buffer is far smaller than the
+    sizes claim, which is safe because nothing is read)."""
+    lib = _lib()
+    buf = torch.zeros(4096, device="cuda", dtype=torch.bfloat16)
+    p = buf.data_ptr()
+    # more than NSB_GEMM_NOALLOC_MAX_TILES tiles in a split launch: 4097 tiles of 128 x 64, 2 splits
+    M = 128 * 4097
+    assert _raw(lib, p, 0, M, 256, 256, 0, 64, 256, 256, p, 64, M, 64, 256, 2) == 2
+    assert b"exceed the maximum" in lib.nsb_gemm_noalloc_error()
+    # output misaligned by 2 bytes
+    assert _raw(lib, p, 0, 128, 64, 64, 0, 64, 64, 64, p + 2, 64, 128, 64, 64, 1) == 1
+    assert b"16-byte aligned" in lib.nsb_gemm_noalloc_error()
+    # a_rows != M
+    assert _raw(lib, p, 0, 127, 64, 64, 0, 64, 64, 64, p, 64, 128, 64, 64, 1) == 1
+    assert b"shapes do not match" in lib.nsb_gemm_noalloc_error()
+    # row stride shorter than the row
+    assert _raw(lib, p, 0, 128, 64, 32, 0, 64, 64, 64, p, 64, 128, 64, 64, 1) == 1
+    assert _raw(lib, p, 0, 128, 64, 64, 0, 64, 64, 56, p, 64, 128, 64, 64, 1) == 1
+    assert b"row stride smaller" in lib.nsb_gemm_noalloc_error()
+    # null operand
+    assert lib.nsb_gemm_bf16_splitk_noalloc(None, 0, 128, 64, 64, p, 0, 64, 64, 64, p, 64, 128, 64, 64, 1,
+                                            None) == 1
+    # reset, then the status word reads zero
+    assert lib.nsb_gemm_noalloc_reset(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    st = ctypes.c_int(-1)
+    assert lib.nsb_gemm_noalloc_status(ctypes.byref(st)) == 0 and st.value == 0
+
+
+@cuda
+def test_noalloc_gemm_unsplit_has_no_tile_limit():
+    """An unsplit product uses no scratch: more tiles than the counter area holds
+    still runs, and matches the torch entry (which may pick another tile plan for
+    this many tiles) and the fp32 product."""
+    from nanospec_b200.ops._ext import cuda_ops
+    lib = _lib()
+    M, N, K = 128 * 4097, 64, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    b = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    ref = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cuda_ops().gemm_test(a, False, b, False, ref, 1)
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    assert _call(lib, a, False, b, False, out, M, N, K, 1) == 0, lib.nsb_gemm_noalloc_error()
+    exact = a.float() @ b.float().t()
+    torch.cuda.synchronize()
+    scale = exact.abs().max().item()
+    assert (out.float() - ref.float()).abs().max().item() <= 1e-2 * scale
+    assert (out.float() - exact).abs().max().item() <= 2e-2 * scale
