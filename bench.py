@@ -364,9 +364,17 @@ class FullWorkload(Workload):
         self.inputs = (ids,)
         self.tokens_per_step = ntrain * args.seq_len
 
-    def step(self, ids):
+    def step(self, ids, phases=None):
         torch.manual_seed(self.args.seed + self.rank)
-        return self.train(ids, self.model, self.o, verifier=self.teacher, optimizer=self.opt)
+        kw = {"phases": phases} if phases is not None else {}
+        return self.train(ids, self.model, self.o, verifier=self.teacher, optimizer=self.opt, **kw)
+
+    def phase_ms(self, dev):
+        """Device ms per phase of one more step (ours only): verifier, draft fwd, head, bwd, AdamW."""
+        from nanospec_b200.utils.phases import PhaseTimer
+        timer = PhaseTimer(dev)
+        self.step(*self.inputs, phases=timer)
+        return {k: round(v, 2) for k, v in timer.summary().items()}
 
     def close(self, world):
         if self.model is not None and world > 1 and hasattr(self.model.sharding, "close_peer"):
@@ -482,6 +490,9 @@ def main():
                    "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
                    "ms_per_step": round(e2e_ms, 3), "wall_ms_per_step": round(wall_ms, 3)}
 
+        phase = None
+        if args.impl == "ours" and full:
+            phase = wl.phase_ms(dev)
         launches = comm_ms = exposed_ms = None
         if args.impl == "ours" and not args.no_count:
             per_step, comm, exposed = profile_step(lambda: wl.step(*inputs))
@@ -538,6 +549,7 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "gpu_launches": launches,
+            "phase_ms_rank0": phase,
             "comm_ms_per_step": None if comm_ms is None or comm_ms != comm_ms else round(comm_ms, 3),
             "exposed_comm_ms_per_step": None if exposed_ms is None or exposed_ms != exposed_ms else round(exposed_ms, 3),
         }

@@ -63,6 +63,9 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, 
                                       at::Tensor dout, int64_t groups);
 int64_t device_error();
 void clear_device_error();
+void head_norm_rope(at::Tensor x, int64_t H, int64_t x_ts, int64_t x_hs, int64_t S, at::Tensor w, double eps,
+                    at::Tensor cs, at::Tensor sn, int64_t rd, at::Tensor y);
+void vattn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor gate, int64_t g_ts, int64_t g_hs, at::Tensor out);
 at::Tensor device_error_tensor();
 void reset_device_error_state();
 }  // namespace ns
@@ -114,6 +117,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_signal", &ns::peer_signal);
   m.def("peer_wait", &ns::peer_wait);
   m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);
+  m.def("head_norm_rope", &ns::head_norm_rope, "(1+w)-RMSNorm per head row + partial RoPE");
+  m.def("vattn_fwd", &ns::vattn_fwd, "causal GQA flash attention (tcgen05) with sigmoid output gate");
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");
   m.def("clear_device_error", &ns::clear_device_error);
   m.def("device_error_tensor", &ns::device_error_tensor, "the error word as a 1-element int32 CUDA view");

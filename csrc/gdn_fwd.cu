@@ -197,21 +197,22 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
     Xv[i * DP + d] *= Bt[i];
   }
 
-  // 3. T = (I + M)^-1, blocked by 16. (a) diagonal blocks: thread c owns column c.
+  // 3. T = (I + M)^-1, blocked by 16. (a) diagonal blocks: thread c owns column c and
+  //    keeps it in registers: T[i][c] = -sum_{m<i} M[i][m] T[m][c] below the diagonal.
   if (tid < C) {
-    const int c = tid, r0 = (c >> 4) * 16;
-    for (int r = r0; r < r0 + 16; ++r) {
-      float t;
-      if (r < c) {
-        t = 0.f;
-      } else if (r == c) {
-        t = 1.f;
-      } else {
-        t = -Ms[r * (C + 1) + c];
-        for (int m = c + 1; m < r; ++m) t -= Ms[r * (C + 1) + m] * Ts[m * (C + 1) + c];
-      }
-      Ts[r * (C + 1) + c] = t;
+    const int c = tid, r0 = (c >> 4) * 16, cl = c & 15;
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = i == cl ? 1.f : 0.f;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) acc = fmaf(Ms[(r0 + i) * (C + 1) + r0 + m], t[m], acc);
+      if (i > cl) t[i] = -acc;
     }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) Ts[(r0 + i) * (C + 1) + c] = t[i];
     for (int r = 0; r < r0; ++r) Ts[r * (C + 1) + c] = 0.f;  // above the diagonal blocks
   }
   __syncthreads();

@@ -63,6 +63,26 @@ inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, 
   return map;
 }
 
+// 3-D bf16 tensor map over [d2][d1][d0] (d0 innermost, contiguous) with element
+// strides s1 (between d1 entries) and s2 (between d2 entries); box = [b2][b1][b0];
+// 128-byte swizzle (b0 * 2 == 128). Used for per-head tiles of [tokens][heads][dim]
+// activations without a transposed copy.
+inline CUtensorMap make_tmap_bf16_3d(const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t s1, int64_t s2,
+                                     int b0, int b1, int b2) {
+  NS_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  NS_CHECK((s1 * 2) % 16 == 0 && (s2 * 2) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)(s1 * 2), (cuuint64_t)(s2 * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  NS_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
 inline int num_sms() {
   static int n = 0;
   if (n == 0) {

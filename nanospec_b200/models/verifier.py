@@ -417,14 +417,12 @@ def attention_forward(attn: QwenAttention, n):
     b, s, _ = n.shape
     d, hq, hk = attn.head_dim, attn.num_heads, attn.num_key_value_heads
     qg = vops.fp8_linear(n, attn.q_proj.weight, attn.q_proj.weight_scale_inv).view(b, s, hq, 2 * d)
-    q, gate = qg[..., :d], qg[..., d:]
-    q = vops.qwen_norm(q, attn.q_norm.weight, attn.q_norm.eps)
     k = vops.fp8_linear(n, attn.k_proj.weight, attn.k_proj.weight_scale_inv).view(b, s, hk, d)
-    k = vops.qwen_norm(k, attn.k_norm.weight, attn.k_norm.eps)
     v = vops.fp8_linear(n, attn.v_proj.weight, attn.v_proj.weight_scale_inv).view(b, s, hk, d)
     pos = torch.arange(s, device=n.device).expand(b, s)
     cos, sin = vops.rotary_factors(pos, attn.rotary_dim, attn.rope_theta, n.dtype)
-    out = vops.causal_attention_gated(q, k, v, gate, cos, sin, attn.rotary_dim)
+    out = vops.gated_attention(qg, k, v, attn.q_norm.weight, attn.k_norm.weight, attn.q_norm.eps, cos, sin,
+                               attn.rotary_dim)
     return vops.fp8_linear(out.reshape(b, s, hq * d), attn.o_proj.weight, attn.o_proj.weight_scale_inv)
 
 

@@ -135,6 +135,41 @@ def causal_attention_gated(q, k, v, gate, cos, sin, rotary_dim):
     return o * gate.sigmoid()
 
 
+def gated_attention(qg, k, v, q_norm_w, k_norm_w, eps, cos, sin, rotary_dim):
+    """The verifier's full-attention mixer after its projections.
+
+    qg [b, s, Hq, 2D] is the interleaved q_proj output (query | output gate per head),
+    k and v [b, s, Hk, D]. Per head: (1+w)-RMSNorm of q and k, partial RoPE on their
+    first ``rotary_dim`` channels, causal GQA softmax attention, then
+    ``out * sigmoid(gate)``; returns [b, s, Hq, D]. Reference statement order:
+    nanospec/train.py:109-136 with nanospec/ops.py:115-126.
+
+    CUDA: one fused norm + RoPE kernel per operand, then the tcgen05 flash-attention
+    kernel (head_dim 64, 128 or 256; the scores never reach HBM). Narrower test
+    heads use the CUDA-core kernel.
+    """
+    b, s, hq, d2 = qg.shape
+    d = d2 // 2
+    hk = k.shape[2]
+    if qg.is_cuda and d in (64, 128, 256):
+        c = _c()
+        qg = qg.contiguous()
+        k = k.contiguous()
+        cs, sn = cos[0].contiguous(), sin[0].contiguous()
+        q_rot = torch.empty(b, s, hq, d, device=qg.device, dtype=qg.dtype)
+        k_rot = torch.empty(b, s, hk, d, device=qg.device, dtype=qg.dtype)
+        c.head_norm_rope(qg, hq, hq * d2, d2, s, q_norm_w, float(eps), cs, sn, int(rotary_dim), q_rot)
+        c.head_norm_rope(k, hk, hk * d, d, s, k_norm_w, float(eps), cs, sn, int(rotary_dim), k_rot)
+        out = torch.empty(b, s, hq, d, device=qg.device, dtype=qg.dtype)
+        gate = qg[..., d:]
+        c.vattn_fwd(q_rot, k_rot, v, gate, hq * d2, d2, out)
+        return out
+    q, gate = qg[..., :d], qg[..., d:]
+    q = qwen_norm(q, q_norm_w, eps)
+    k = qwen_norm(k, k_norm_w, eps)
+    return causal_attention_gated(q, k, v, gate, cos, sin, rotary_dim)
+
+
 def gated_delta_rule_backward(q, k, v, g, beta, dout, groups=1):
     """Gradients (dq, dk, dv, dg, dbeta) of the gated delta rule w.r.t. its raw inputs.
 

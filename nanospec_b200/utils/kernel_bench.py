@@ -172,8 +172,9 @@ def bench_gdn(a):
     bus = _time(lambda: vops.gated_delta_rule_backward(q, k, v, g, beta, dout, nv // nk), a.reps, a.warmup)
     # chunked form, chunk 64: per head about 4*S*64*d (intra-chunk) + 4*S*d*d (state) MACs forward
     flops = 2.0 * nv * (4 * s * 64 * d + 4 * s * d * d)
+    kern = _kernel_times(lambda: vops.gated_delta_rule(q, k, v, g, beta, nv // nk))
     return {"op": "gdn_chunk", "S": s, "heads": nv, "fwd_us": round(us, 1), "bwd_us": round(bus, 1),
-            "fwd_tflops": round(flops / us / 1e6, 2)}
+            "fwd_tflops": round(flops / us / 1e6, 2), "fwd_kernels_us": kern}
 
 
 def bench_verifier(a):
@@ -188,7 +189,7 @@ def bench_verifier(a):
                    config=synthetic_hf_config(tc))
     ids = torch.randint(0, tc["vocab_size"], (1, a.S), device="cuda")
     names = ("embedding", "add", "silu_mul", "qwen_norm", "qwen_gated_norm", "fp8_linear", "causal_conv_silu",
-             "gdn_gates", "gated_delta_rule", "causal_attention_gated")
+             "gdn_gates", "gated_delta_rule", "causal_attention_gated", "gated_attention")
     times, orig = {}, {n: getattr(vops, n) for n in names}
 
     def wrap(name, fn):
@@ -226,6 +227,23 @@ def _verifier_fp8_flops(tc, s):
             if quant and len(shape) == 2:
                 total += 2.0 * s * shape[0] * shape[1]
     return total
+
+
+def _kernel_times(fn, reps=3):
+    """Mean device microseconds per call of every kernel ``fn`` launches (torch.profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    fn()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    out = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            name = e.name.split("(")[0].split("<")[0].replace("void ", "").strip()
+            out[name] = out.get(name, 0.0) + e.device_time_total / reps
+    return {k: round(v, 1) for k, v in sorted(out.items(), key=lambda kv: -kv[1])}
 
 
 def _graph_time(fns, reps):

@@ -123,3 +123,48 @@ def test_gated_delta_rule_backward(D, s, groups):
     got = vops.gated_delta_rule_backward(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), dout.cuda(), groups)
     for name, x, y in zip(("dq", "dk", "dv", "dg", "dbeta"), got, expect):
         close(x, y, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+@pytest.mark.parametrize("D,rd,hq,hk,s,b", [(64, 32, 4, 2, 200, 2), (128, 64, 4, 4, 130, 1),
+                                          (256, 64, 6, 2, 150, 2), (256, 64, 24, 4, 640, 1)])
+def test_gated_attention_tensor_core_path(D, rd, hq, hk, s, b):
+    """Fused norm + partial RoPE + tcgen05 flash attention + sigmoid gate vs the CPU
+    statements (qwen_norm, partial_rope, bf16 scores, fp32 softmax, bf16 P @ V)."""
+    qg = torch.randn(b, s, hq, 2 * D).bfloat16()
+    k = torch.randn(b, s, hk, D).bfloat16()
+    v = torch.randn(b, s, hk, D).bfloat16()
+    wq = (torch.randn(D) * 0.1).bfloat16()
+    wk = (torch.randn(D) * 0.1).bfloat16()
+    pos = torch.arange(s).expand(b, s)
+    cos, sin = ref.rotary_factors(pos, rd, 1e7, torch.bfloat16)
+    expect = vops.gated_attention(qg, k, v, wq, wk, 1e-6, cos, sin, rd)
+    got = vops.gated_attention(qg.cuda(), k.cuda(), v.cuda(), wq.cuda(), wk.cuda(), 1e-6, cos.cuda(), sin.cuda(), rd)
+    close(got, expect, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+def test_gated_attention_large_logits_rescale():
+    """Large, growing scores (norm weight 3 gives logits of std ~20) force the kernel's
+    running-maximum rescale of O in TMEM. Oracle: the same normalised, RoPE'd q / k
+    with fp32 scores and softmax (the bf16-score statement is too coarse at this scale)."""
+    b, s, hq, hk, D, rd = 1, 384, 2, 1, 128, 32
+    qg = torch.randn(b, s, hq, 2 * D).bfloat16()
+    k = torch.randn(b, s, hk, D).bfloat16()
+    v = torch.randn(b, s, hk, D).bfloat16()
+    w = torch.full((D,), 3.0).bfloat16()
+    pos = torch.arange(s).expand(b, s)
+    cos, sin = ref.rotary_factors(pos, rd, 1e7, torch.bfloat16)
+    q = ref.partial_rope(vops.qwen_norm(qg[..., :D], w, 1e-6), cos, sin, rd)
+    kr = ref.partial_rope(vops.qwen_norm(k, w, 1e-6), cos, sin, rd)
+    g = hq // hk
+    qt = q.float().transpose(1, 2)
+    kt = kr.float().repeat_interleave(g, 2).transpose(1, 2)
+    vt = v.float().repeat_interleave(g, 2).transpose(1, 2)
+    sc = (qt @ kt.transpose(-1, -2)) * D ** -0.5
+    assert sc.std() > 10  # the rescale path is exercised
+    sc = sc.masked_fill(torch.ones(s, s, dtype=torch.bool).triu(1), float("-inf"))
+    o = (sc.softmax(-1) @ vt).transpose(1, 2).bfloat16()
+    expect = o * qg[..., D:].sigmoid()
+    got = vops.gated_attention(qg.cuda(), k.cuda(), v.cuda(), w.cuda(), w.cuda(), 1e-6, cos.cuda(), sin.cuda(), rd)
+    close(got, expect, rtol=3e-2, cos_min=0.999)
