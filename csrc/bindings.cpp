@@ -63,6 +63,14 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, 
                                       at::Tensor dout, int64_t groups);
 int64_t device_error();
 void clear_device_error();
+void fp8_gemm(at::Tensor q, at::Tensor sa, at::Tensor w, at::Tensor scale_inv, at::Tensor out);
+void quant_e4m3(at::Tensor x, at::Tensor q, at::Tensor s);
+void add_norm(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps, c10::optional<at::Tensor> x_out,
+              c10::optional<at::Tensor> n_out, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> s_out);
+void silu_mul_quant(at::Tensor gu, at::Tensor q, at::Tensor s);
+void gated_norm_quant(at::Tensor x, at::Tensor z, int64_t nv, int64_t z_ts, at::Tensor w, double eps, at::Tensor q,
+                      at::Tensor s);
+void conv_silu_vec(at::Tensor x, int64_t ld, at::Tensor w, at::Tensor y);
 void head_norm_rope(at::Tensor x, int64_t H, int64_t x_ts, int64_t x_hs, int64_t S, at::Tensor w, double eps,
                     at::Tensor cs, at::Tensor sn, int64_t rd, at::Tensor y);
 void vattn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor gate, int64_t g_ts, int64_t g_hs, at::Tensor out);
@@ -117,6 +125,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_signal", &ns::peer_signal);
   m.def("peer_wait", &ns::peer_wait);
   m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);
+  m.def("fp8_gemm", &ns::fp8_gemm, "block-scaled FP8 GEMM of pre-quantised activations");
+  m.def("quant_e4m3", &ns::quant_e4m3);
+  m.def("add_norm", &ns::add_norm, py::arg("x"), py::arg("y"), py::arg("w"), py::arg("eps"), py::arg("x_out"),
+        py::arg("n_out"), py::arg("q_out"), py::arg("s_out"));
+  m.def("silu_mul_quant", &ns::silu_mul_quant);
+  m.def("gated_norm_quant", &ns::gated_norm_quant);
+  m.def("conv_silu_vec", &ns::conv_silu_vec);
   m.def("head_norm_rope", &ns::head_norm_rope, "(1+w)-RMSNorm per head row + partial RoPE");
   m.def("vattn_fwd", &ns::vattn_fwd, "causal GQA flash attention (tcgen05) with sigmoid output gate");
   m.def("device_error", &ns::device_error, "read the kernels' bounded-wait error word");

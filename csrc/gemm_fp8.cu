@@ -223,23 +223,20 @@ static CUtensorMap make_tmap_u8(const void* base, int64_t rows, int64_t cols, in
   return map;
 }
 
-// Quantise x, then the block-scaled GEMM. Also returns nothing: writes out [T, N] bf16.
-void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out) {
-  check_bf16(x, "x");
-  NS_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "fp8_linear: contiguous tensors expected");
+// out [T, N] bf16 = block-scaled GEMM of pre-quantised activations q [T, K] (e4m3 codes
+// as uint8) with scales sa [T, K/128] and e4m3 weights w [N, K] with scale_inv
+// [N/128, K/128].
+void fp8_gemm(at::Tensor q, at::Tensor sa, at::Tensor w, at::Tensor scale_inv, at::Tensor out) {
+  NS_CHECK(q.is_contiguous() && w.is_contiguous() && sa.is_contiguous(), "fp8_gemm: contiguous operands expected");
+  NS_CHECK(out.stride(1) == 1, "fp8_gemm: output rows must be contiguous");
   NS_CHECK(w.scalar_type() == at::kFloat8_e4m3fn, "weight must be float8_e4m3fn");
-  const int64_t T = x.size(0);
-  const int K = x.size(1), N = w.size(0);
+  const int64_t T = q.size(0);
+  const int K = q.size(1), N = w.size(0);
   NS_CHECK(K % 128 == 0 && N % 128 == 0 && w.size(1) == K, "FP8 weights need 128 x 128 blocks");
   NS_CHECK(scale_inv.scalar_type() == at::kFloat && scale_inv.size(0) == N / 128 && scale_inv.size(1) == K / 128,
            "weight_scale_inv must be fp32 [N/128, K/128]");
+  NS_CHECK(sa.scalar_type() == at::kFloat && sa.size(0) == T && sa.size(1) == K / 128, "sa must be fp32 [T, K/128]");
   if (T == 0) return;
-  auto q = at::empty({T, K}, x.options().dtype(at::kByte));
-  auto sa = at::empty({T, K / 128}, x.options().dtype(at::kFloat));
-  const int64_t warps = T * (K / 128);
-  quant_e4m3_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), T, K, q.data_ptr<uint8_t>(), sa.data_ptr<float>());
-  NS_CUDA(cudaGetLastError());
   CUtensorMap ta = make_tmap_u8(q.data_ptr(), T, K, F8_BM);
   CUtensorMap tb = make_tmap_u8(w.data_ptr(), N, K, F8_BN);
   F8Args a{};
@@ -258,6 +255,32 @@ void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out
   dim3 grid((unsigned)((T + F8_BM - 1) / F8_BM), (unsigned)(N / F8_BN));
   fp8_gemm_kernel<<<grid, 192, F8_SMEM, stream()>>>(ta, tb, a);
   NS_CUDA(cudaGetLastError());
+}
+
+// 1 x 128 dynamic quantisation of bf16 rows x [T, K] into q (uint8 e4m3 codes) and s.
+void quant_e4m3(at::Tensor x, at::Tensor q, at::Tensor s) {
+  check_bf16(x, "x");
+  NS_CHECK(x.is_contiguous() && x.size(1) % 128 == 0, "quant_e4m3: contiguous rows of 128-multiples");
+  const int64_t T = x.size(0);
+  const int K = x.size(1);
+  const int64_t warps = T * (K / 128);
+  if (warps == 0) return;
+  quant_e4m3_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), T, K, q.data_ptr<uint8_t>(), s.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+}
+
+// Quantise x, then the block-scaled GEMM: writes out [T, N] bf16.
+void fp8_linear(at::Tensor x, at::Tensor w, at::Tensor scale_inv, at::Tensor out) {
+  check_bf16(x, "x");
+  NS_CHECK(x.is_contiguous() && out.is_contiguous(), "fp8_linear: contiguous tensors expected");
+  const int64_t T = x.size(0);
+  const int K = x.size(1);
+  if (T == 0) return;
+  auto q = at::empty({T, K}, x.options().dtype(at::kByte));
+  auto sa = at::empty({T, K / 128}, x.options().dtype(at::kFloat));
+  quant_e4m3(x, q, sa);
+  fp8_gemm(q, sa, w, scale_inv, out);
 }
 
 }  // namespace ns

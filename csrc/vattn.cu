@@ -432,9 +432,9 @@ void vattn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor gate, int64_
   check_bf16(k, "k");
   check_bf16(v, "v");
   NS_CHECK(q.is_contiguous() && out.is_contiguous(), "vattn_fwd: q and out must be contiguous");
-  NS_CHECK(k.stride(3) == 1 && v.stride(3) == 1 && k.stride(1) == k.size(2) * k.stride(2) &&
-               v.stride(1) == v.size(2) * v.stride(2),
-           "vattn_fwd: k / v rows must be [tokens][heads][D] with unit channel stride");
+  NS_CHECK(k.stride(3) == 1 && v.stride(3) == 1 && k.stride(0) == k.size(1) * k.stride(1) &&
+               v.stride(0) == v.size(1) * v.stride(1),
+           "vattn_fwd: k / v must be [tokens][heads][D] views with unit channel stride and one token stride");
   NS_CHECK(q.size(2) % k.size(2) == 0, "query heads must be a multiple of key heads");
   if (q.size(1) == 0) return;
   switch (q.size(3)) {

@@ -1,0 +1,306 @@
+// Fused producers of the verifier's FP8 projections (forward only).
+//
+// The reference quantises every projection input on its own (nanospec/ops.py:183-200:
+// 1 x 128 blocks, scale = amax / 448, e4m3) after separate residual-add, norm and
+// SwiGLU passes (nanospec/train.py:137-153). Here the kernel that produces an
+// activation also emits its e4m3 codes and 1 x 128 scales, so the FP8 GEMM reads
+// 1 byte per element and no separate quantisation pass runs:
+//
+//  * add_norm_kernel: x' = bf16(x + y) (y optional), n = bf16(x' * rsqrt(mean(x'^2)
+//    + eps) * (1 + w)); writes x', and n as bf16 and/or e4m3 + scales. One CTA of
+//    256 threads per token row, 8 channels (16 bytes) per access; a 128-channel
+//    quantisation block is 16 consecutive chunks held by 16 consecutive lanes.
+//  * silu_mul_quant_kernel: h = bf16(bf16(silu(gate)) * up) from the fused [gate | up]
+//    projection, emitted as e4m3 + scales (one warp per 128-channel block).
+//  * gated_norm_quant_kernel: w * bf16(rmsnorm(o)) * silu(z) per 128-wide value head
+//    (one warp per head row = one quantisation block).
+//  * conv_silu_vec_kernel: causal depthwise conv (kernel K <= 4) + SiLU, 8 channels
+//    per thread.
+// Quantisation follows the reference statement on the bf16 value v:
+// s = amax / 448, q = e4m3(clamp(v / max(s, FLT_MIN), -448, 448)) (saturating).
+#include "common.h"
+#include "sm100.cuh"
+
+#include <cuda_fp8.h>
+
+namespace ns {
+
+using bf16 = __nv_bfloat16;
+
+namespace vf {
+
+__device__ __forceinline__ float rb(float x) { return sm100::bf16_round(x); }
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p = __bfloat1622float2(h[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+// Division as in the reference (v / s), kept exact: the reciprocal would round differently.
+__device__ __forceinline__ uint32_t e4m3x4_div(float a, float b, float c, float d, float den) {
+  const float v[4] = {a, b, c, d};
+  uint32_t p = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float y = fminf(fmaxf(v[i] / den, -448.f), 448.f);
+    p |= (uint32_t)__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+  }
+  return p;
+}
+
+constexpr int AN_THREADS = 256;
+constexpr int AN_MAX_CPT = 4;  // chunks of 8 per thread: rows up to 8192 channels
+
+__global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ y,
+                                                              const bf16* __restrict__ w, float eps, int H,
+                                                              bf16* __restrict__ x_out, bf16* __restrict__ n_out,
+                                                              uint8_t* __restrict__ q_out, float* __restrict__ s_out) {
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nch = H / 8;
+  float v[AN_MAX_CPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < AN_MAX_CPT; ++j) {
+    const int c = tid + j * AN_THREADS;
+    if (c < nch) {
+      unpack8(reinterpret_cast<const uint4*>(x + row * H)[c], v[j]);
+      if (y) {
+        float t[8];
+        unpack8(reinterpret_cast<const uint4*>(y + row * H)[c], t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = rb(v[j][i] + t[i]);
+        reinterpret_cast<uint4*>(x_out + row * H)[c] = pack8(v[j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+    }
+  }
+  __shared__ float red[AN_THREADS / 32];
+  __shared__ float tot;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float t = tid < AN_THREADS / 32 ? red[tid] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
+    if (tid == 0) tot = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(tot / H + eps);
+  const int kbs = H / 128;
+#pragma unroll
+  for (int j = 0; j < AN_MAX_CPT; ++j) {
+    if (j * AN_THREADS >= nch) break;  // uniform across the block
+    const int c = tid + j * AN_THREADS;
+    const bool in = c < nch;
+    float nv[8];
+    if (in) {
+      float wv[8];
+      unpack8(reinterpret_cast<const uint4*>(w)[c], wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) nv[i] = rb(v[j][i] * inv * (1.f + wv[i]));
+      if (n_out) reinterpret_cast<uint4*>(n_out + row * H)[c] = pack8(nv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) nv[i] = 0.f;
+    }
+    if (q_out) {  // a 128-channel block is 16 chunks on 16 consecutive lanes
+      float am = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(nv[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffff, am, o, 16));
+      const float s = am / 448.f;
+      const float den = fmaxf(s, 1.17549435e-38f);
+      if (in) {
+        uint2 pk;
+        pk.x = e4m3x4_div(nv[0], nv[1], nv[2], nv[3], den);
+        pk.y = e4m3x4_div(nv[4], nv[5], nv[6], nv[7], den);
+        reinterpret_cast<uint2*>(q_out + row * H)[c] = pk;
+        if ((c & 15) == 0) s_out[row * kbs + (c >> 4)] = s;
+      }
+    }
+  }
+}
+
+// gu [T, 2m] = [gate | up]; h = bf16(bf16(silu(gate)) * up) -> e4m3 + scales [T, m/128]
+__global__ void silu_mul_quant_kernel(const bf16* __restrict__ gu, int64_t T, int m, uint8_t* __restrict__ q,
+                                      float* __restrict__ s) {
+  const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kbs = m / 128;
+  if (wid >= T * kbs) return;
+  const int64_t t = wid / kbs;
+  const int kb = (int)(wid % kbs);
+  const bf16* g = gu + t * 2 * m + kb * 128 + lane * 4;
+  const bf16* u = g + m;
+  const uint2 gr = *reinterpret_cast<const uint2*>(g), ur = *reinterpret_cast<const uint2*>(u);
+  const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gr);
+  const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&ur);
+  float h[4];
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float2 gf = __bfloat1622float2(gh[i]), uf = __bfloat1622float2(uh[i]);
+    const float a = rb(rb(gf.x / (1.f + expf(-gf.x))) * uf.x);
+    const float b = rb(rb(gf.y / (1.f + expf(-gf.y))) * uf.y);
+    h[2 * i] = a;
+    h[2 * i + 1] = b;
+    am = fmaxf(am, fmaxf(fabsf(a), fabsf(b)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffff, am, o));
+  const float sc = am / 448.f;
+  const float den = fmaxf(sc, 1.17549435e-38f);
+  *reinterpret_cast<uint32_t*>(q + t * m + kb * 128 + lane * 4) = e4m3x4_div(h[0], h[1], h[2], h[3], den);
+  if (lane == 0) s[t * kbs + kb] = sc;
+}
+
+// rows of 128 (row = token * nv + head): y = bf16(rb(w * rb(x * inv)) * silu(z)) ->
+// e4m3 + one scale per row; z(token, head) at z + token * z_ts + head * 128.
+__global__ void gated_norm_quant_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int nv, int64_t z_ts,
+                                        const bf16* __restrict__ w, int64_t rows, float eps, uint8_t* __restrict__ q,
+                                        float* __restrict__ s) {
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint2 xr = *reinterpret_cast<const uint2*>(x + row * 128 + lane * 4);
+  const uint2 zr = *reinterpret_cast<const uint2*>(z + (row / nv) * z_ts + (row % nv) * 128 + lane * 4);
+  const uint2 wr = *reinterpret_cast<const uint2*>(w + lane * 4);
+  const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xr);
+  const __nv_bfloat162* zh = reinterpret_cast<const __nv_bfloat162*>(&zr);
+  const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wr);
+  float xv[4], zv[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float2 a = __bfloat1622float2(xh[i]), b = __bfloat1622float2(zh[i]), c = __bfloat1622float2(wh[i]);
+    xv[2 * i] = a.x, xv[2 * i + 1] = a.y, zv[2 * i] = b.x, zv[2 * i + 1] = b.y, wv[2 * i] = c.x, wv[2 * i + 1] = c.y;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss += xv[i] * xv[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  const float inv = rsqrtf(ss / 128.f + eps);
+  float y[4];
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float sg = zv[i] / (1.f + expf(-zv[i]));
+    y[i] = rb(rb(wv[i] * rb(xv[i] * inv)) * sg);
+    am = fmaxf(am, fabsf(y[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffff, am, o));
+  const float sc = am / 448.f;
+  const float den = fmaxf(sc, 1.17549435e-38f);
+  *reinterpret_cast<uint32_t*>(q + row * 128 + lane * 4) = e4m3x4_div(y[0], y[1], y[2], y[3], den);
+  if (lane == 0) s[row] = sc;
+}
+
+// out[b, t, c] = silu(bf16(sum_j w[c, j] x[b, t - (K-1) + j, c])); x rows of ld elements
+// (the first C channels of each row are convolved), 8 channels per thread.
+__global__ void conv_silu_vec_kernel(const bf16* __restrict__ x, int64_t ld, const bf16* __restrict__ w,
+                                     bf16* __restrict__ y, int s, int C, int K, int64_t total8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % (C / 8));
+    const int64_t bt = i / (C / 8);
+    const int t = (int)(bt % s);
+    const int c = c8 * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < K; ++j) {
+      const int tt = t - (K - 1) + j;
+      if (tt < 0) continue;
+      float xv[8];
+      unpack8(*reinterpret_cast<const uint4*>(x + (bt - t + tt) * ld + c), xv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(w[(c + e) * K + j]) * xv[e];
+    }
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float zz = rb(acc[e]);
+      o[e] = zz / (1.f + expf(-zz));
+    }
+    reinterpret_cast<uint4*>(y + bt * C)[c8] = pack8(o);
+  }
+}
+
+}  // namespace vf
+
+static int grid_for(int64_t threads) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((threads + 255) / 256, (int64_t)num_sms() * 32));
+}
+
+// x_out / n_out / q_out+s_out optional (undefined tensors); y optional.
+void add_norm(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps, c10::optional<at::Tensor> x_out,
+              c10::optional<at::Tensor> n_out, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> s_out) {
+  check_bf16(x, "x");
+  const int H = (int)x.size(-1);
+  const int64_t rows = x.numel() / H;
+  NS_CHECK(x.is_contiguous() && H % 8 == 0 && H / 8 <= vf::AN_THREADS * vf::AN_MAX_CPT, "add_norm: row width");
+  NS_CHECK(!q_out || H % 128 == 0, "add_norm: quantised output needs 128-multiple rows");
+  NS_CHECK(!y || x_out, "add_norm: the residual sum needs x_out");
+  if (rows == 0) return;
+  auto p = [](const c10::optional<at::Tensor>& t) -> void* { return t ? t->data_ptr() : nullptr; };
+  vf::add_norm_kernel<<<(unsigned)rows, vf::AN_THREADS, 0, stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(p(y)),
+      reinterpret_cast<const bf16*>(w.data_ptr()), (float)eps, H, reinterpret_cast<bf16*>(p(x_out)),
+      reinterpret_cast<bf16*>(p(n_out)), reinterpret_cast<uint8_t*>(p(q_out)), reinterpret_cast<float*>(p(s_out)));
+  NS_CUDA(cudaGetLastError());
+}
+
+void silu_mul_quant(at::Tensor gu, at::Tensor q, at::Tensor s) {
+  check_bf16(gu, "gu");
+  const int64_t T = gu.size(0);
+  const int m = (int)(gu.size(1) / 2);
+  NS_CHECK(gu.is_contiguous() && m % 128 == 0, "silu_mul_quant: [T, 2m] with m a multiple of 128");
+  const int64_t warps = T * (m / 128);
+  if (warps == 0) return;
+  vf::silu_mul_quant_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream()>>>(
+      reinterpret_cast<const bf16*>(gu.data_ptr()), T, m, q.data_ptr<uint8_t>(), s.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+}
+
+// x [T * nv, 128] contiguous; z token rows of stride z_ts elements, head h at + h * 128.
+void gated_norm_quant(at::Tensor x, at::Tensor z, int64_t nv, int64_t z_ts, at::Tensor w, double eps, at::Tensor q,
+                      at::Tensor s) {
+  NS_CHECK(x.size(-1) == 128 && x.is_contiguous(), "gated_norm_quant: contiguous rows of 128");
+  NS_CHECK(z_ts % 8 == 0, "gated_norm_quant: z rows 16-byte aligned");
+  const int64_t rows = x.numel() / 128;
+  if (rows == 0) return;
+  vf::gated_norm_quant_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(z.data_ptr()), (int)nv, z_ts,
+      reinterpret_cast<const bf16*>(w.data_ptr()), rows, (float)eps, q.data_ptr<uint8_t>(), s.data_ptr<float>());
+  NS_CUDA(cudaGetLastError());
+}
+
+// x: [b, s, *] rows of row stride ld (elements); the first C channels are convolved.
+void conv_silu_vec(at::Tensor x, int64_t ld, at::Tensor w, at::Tensor y) {
+  const int b = (int)y.size(0), s = (int)y.size(1), C = (int)y.size(2), K = (int)w.size(1);
+  NS_CHECK(C % 8 == 0 && ld % 8 == 0 && y.is_contiguous(), "conv_silu_vec: 8-channel alignment");
+  const int64_t total8 = (int64_t)b * s * (C / 8);
+  if (total8 == 0) return;
+  vf::conv_silu_vec_kernel<<<grid_for(total8), 256, 0, stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), ld, reinterpret_cast<const bf16*>(w.data_ptr()),
+      reinterpret_cast<bf16*>(y.data_ptr()), s, C, K, total8);
+  NS_CUDA(cudaGetLastError());
+}
+
+}  // namespace ns

@@ -139,6 +139,10 @@ def main(argv=None):
     if data is not None and (data.ndim != 2 or data.shape[1] != args.seq_len or len(data) < node.train_gpus):
         raise ValueError("--tokens needs at least train_gpus rows with --seq-len columns")
     rows = []
+    periodic = None
+    if args.save_every and model is not None:
+        periodic = checkpoint.Periodic(str(Path(args.output).with_suffix("")) + "-checkpoint", model, opt, o,
+                                       every=args.save_every, keep=2)
     for offset in range(args.steps):
         step = start + offset
         if data is None:
@@ -187,11 +191,13 @@ def main(argv=None):
             rows.append(row)
             if node.rank == 0:
                 print(json.dumps(row), flush=True)
-            if args.save_every and (step + 1) % args.save_every == 0 and offset + 1 < args.steps:
-                checkpoint.save(str(Path(args.output).with_suffix("")) + "-checkpoint", model, opt, o, step + 1)
+            if periodic is not None and offset + 1 < args.steps:
+                periodic.step(step + 1)  # asynchronous: host staging overlaps the next steps
         if world > 1:
             dist.barrier()
     ckpt_path = None
+    if periodic is not None:
+        periodic.close()
     if node.training:
         ckpt_path = checkpoint.save(str(Path(args.output).with_suffix("")) + "-checkpoint", model, opt, o,
                                     start + args.steps)

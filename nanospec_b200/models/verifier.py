@@ -335,6 +335,57 @@ class QwenStage(nn.Module):
         self.norm = _W(w["norm.weight"], tc["rms_norm_eps"]) if last else None
         self.lm_head = _W(w["lm_head.weight"]) if last else None
         self.eval()
+        self.fused = False
+        if torch.device(device).type == "cuda":
+            fuse_projections(self)
+            self.fused = _fused_ok(self)
+
+
+def _is_fp8(lin) -> bool:
+    w = lin.weight
+    return w.dtype == torch.float8_e4m3fn and w.shape[0] % 128 == 0 and w.shape[1] % 128 == 0
+
+
+@torch.no_grad()
+def _fuse(parts):
+    """One projection over adjacent weights (same input): the parts become row views of
+    the fused weight and scale, so the memory is not duplicated."""
+    w = torch.cat([p.weight for p in parts], 0)
+    fp8 = parts[0].weight_scale_inv is not None
+    sc = torch.cat([p.weight_scale_inv for p in parts], 0) if fp8 else None
+    r = 0
+    for p in parts:
+        n = p.weight.shape[0]
+        p.weight = nn.Parameter(w[r:r + n], requires_grad=False)
+        if fp8:
+            p.weight_scale_inv = sc[r // 128:(r + n) // 128]
+        r += n
+    return FP8Linear(w, sc)
+
+
+def fuse_projections(stage: "QwenStage"):
+    """Concatenate projections that read the same input (once, on CUDA stages):
+    GDN [in_proj_qkv; in_proj_z] and [in_proj_b; in_proj_a], attention [q; k; v], MLP
+    [gate; up]. The fused forward runs one GEMM for each group."""
+    for layer in stage.layers:
+        a = layer.linear_attn
+        if a is not None and _is_fp8(a.in_proj_qkv) and _is_fp8(a.in_proj_z):
+            a.in_proj_qkvz = _fuse([a.in_proj_qkv, a.in_proj_z])
+            a.in_proj_ba = _fuse([a.in_proj_b, a.in_proj_a])
+        t = layer.self_attn
+        if t is not None and all(_is_fp8(p) for p in (t.q_proj, t.k_proj, t.v_proj)):
+            t.qkv = _fuse([t.q_proj, t.k_proj, t.v_proj])
+        m = layer.mlp
+        if _is_fp8(m.gate_proj) and _is_fp8(m.up_proj) and _is_fp8(m.down_proj):
+            m.gate_up = _fuse([m.gate_proj, m.up_proj])
+
+
+def _fused_ok(stage) -> bool:
+    return all(getattr(l.mlp, "gate_up", None) is not None and
+               (getattr(l.linear_attn, "in_proj_qkvz", None) is not None if l.linear_attn is not None
+                else getattr(l.self_attn, "qkv", None) is not None)
+               for l in stage.layers) and stage.config["hidden_size"] % 128 == 0 and \
+        stage.config.get("linear_value_head_dim", 128) == 128
 
 
 def synthetic_hf_config(text_config: dict, *, seed=0, fp8=True) -> dict:
@@ -427,6 +478,81 @@ def attention_forward(attn: QwenAttention, n):
 
 
 @torch.no_grad()
+def _gdn_fused(attn: QwenGatedDeltaNet, n_bf, nq, b, s):
+    nk, nv = attn.num_key_heads, attn.num_value_heads
+    dk, dv = attn.key_head_dim, attn.value_head_dim
+    conv = 2 * nk * dk + nv * dv
+    mixed = vops.fp8_gemm(nq[0], nq[1], attn.in_proj_qkvz.weight, attn.in_proj_qkvz.weight_scale_inv)
+    ba = vops.fp8_linear(n_bf, attn.in_proj_ba.weight, None)
+    total = mixed.shape[1]
+    qkv = vops.causal_conv_silu_rows(mixed.view(b, s, total), total, attn.conv1d.weight, conv)
+    q, k, v = qkv.split((nk * dk, nk * dk, nv * dv), -1)
+    g, beta = vops.gdn_gates(ba[:, nv:].contiguous(), ba[:, :nv].contiguous(), attn.A_log, attn.dt_bias)
+    o = vops.gated_delta_rule(q.reshape(b, s, nk, dk), k.reshape(b, s, nk, dk), v.reshape(b, s, nv, dv),
+                              g.view(b, s, nv), beta.view(b, s, nv), nv // nk)
+    oq = vops.gated_norm_quantize(o.view(-1, dv), mixed[:, conv:], nv, total, attn.norm.weight, attn.norm.eps)
+    return vops.fp8_gemm(oq[0].view(b * s, nv * dv), oq[1].view(b * s, nv), attn.out_proj.weight,
+                         attn.out_proj.weight_scale_inv)
+
+
+@torch.no_grad()
+def _attention_fused(attn: QwenAttention, nq, b, s, device, dtype):
+    d, hq, hk = attn.head_dim, attn.num_heads, attn.num_key_value_heads
+    qkv = vops.fp8_gemm(nq[0], nq[1], attn.qkv.weight, attn.qkv.weight_scale_inv)
+    total = qkv.shape[1]
+    qkv3 = qkv.view(b, s, total)
+    qg = qkv3[..., :2 * hq * d].unflatten(-1, (hq, 2 * d))
+    k = qkv3[..., 2 * hq * d:2 * hq * d + hk * d].unflatten(-1, (hk, d))
+    v = qkv3[..., 2 * hq * d + hk * d:].unflatten(-1, (hk, d))
+    pos = torch.arange(s, device=device).expand(b, s)
+    cos, sin = vops.rotary_factors(pos, attn.rotary_dim, attn.rope_theta, dtype)
+    out = vops.gated_attention(qg, k, v, attn.q_norm.weight, attn.k_norm.weight, attn.q_norm.eps, cos, sin,
+                               attn.rotary_dim)
+    oq = vops.quantize(out.view(b * s, hq * d))
+    return vops.fp8_gemm(oq[0], oq[1], attn.o_proj.weight, attn.o_proj.weight_scale_inv)
+
+
+@torch.no_grad()
+def _stage_forward_fused(stage: QwenStage, x, capture, on_capture):
+    """CUDA forward with fused projections and fused producers: every residual add is
+    fused with the following (1+w)-RMSNorm, and every FP8 projection input leaves its
+    producer already quantised (e4m3 + 1 x 128 scales). Same math as the statement
+    path below; only roundings inside fp32 reductions differ."""
+    b, s, h = x.shape
+    layers = list(stage.layers)
+    ln = layers[0].input_layernorm
+    _, n_bf, nq = vops.add_norm(x, None, ln.weight, ln.eps, want_bf16=layers[0].linear_attn is not None,
+                                want_q=True)
+    captured = {}
+    for i, layer in enumerate(layers):
+        li = stage.start + i
+        if layer.linear_attn is not None:
+            out = _gdn_fused(layer.linear_attn, n_bf.view(b * s, h), (nq[0], nq[1]), b, s)
+        else:
+            out = _attention_fused(layer.self_attn, nq, b, s, x.device, x.dtype)
+        pl = layer.post_attention_layernorm
+        x, _, n2q = vops.add_norm(x, out.view(b, s, h), pl.weight, pl.eps, want_bf16=False, want_q=True)
+        mlp = layer.mlp
+        gu = vops.fp8_gemm(n2q[0], n2q[1], mlp.gate_up.weight, mlp.gate_up.weight_scale_inv)
+        hq = vops.silu_mul_quantize(gu)
+        down = vops.fp8_gemm(hq[0], hq[1], mlp.down_proj.weight, mlp.down_proj.weight_scale_inv).view(b, s, h)
+        if i + 1 < len(layers):
+            nxt = layers[i + 1]
+            ln = nxt.input_layernorm
+            x, n_bf, nq = vops.add_norm(x, down, ln.weight, ln.eps, want_bf16=nxt.linear_attn is not None,
+                                        want_q=True)
+        elif stage.norm is not None:
+            x, final, _ = vops.add_norm(x, down, stage.norm.weight, stage.norm.eps)
+        else:
+            x = vops.add(x, down)
+        if li in capture:
+            captured[li] = x
+            if on_capture is not None:
+                on_capture(li, x)
+    return (final if stage.norm is not None else x), captured
+
+
+@torch.no_grad()
 def stage_forward(stage: QwenStage, x_or_ids, capture=(), on_capture=None):
     """Run the stage's layers. Returns (output, {layer_index: hidden}).
 
@@ -438,6 +564,8 @@ def stage_forward(stage: QwenStage, x_or_ids, capture=(), on_capture=None):
         x = vops.embedding(x_or_ids, stage.embed_tokens.weight)
     else:
         x = x_or_ids
+    if getattr(stage, "fused", False) and x.is_cuda and len(stage.layers) > 0:
+        return _stage_forward_fused(stage, x, capture, on_capture)
     captured = {}
     for li, layer in enumerate(stage.layers, start=stage.start):
         n = vops.qwen_norm(x, layer.input_layernorm.weight, layer.input_layernorm.eps)

@@ -151,23 +151,80 @@ def gated_attention(qg, k, v, q_norm_w, k_norm_w, eps, cos, sin, rotary_dim):
     b, s, hq, d2 = qg.shape
     d = d2 // 2
     hk = k.shape[2]
-    if qg.is_cuda and d in (64, 128, 256):
+    if qg.is_cuda and d in (64, 128, 256) and qg.stride(-1) == 1 and k.stride(-1) == 1 and v.stride(-1) == 1:
+        # q / gate / k / v may be strided views of one fused projection output
         c = _c()
-        qg = qg.contiguous()
-        k = k.contiguous()
         cs, sn = cos[0].contiguous(), sin[0].contiguous()
         q_rot = torch.empty(b, s, hq, d, device=qg.device, dtype=qg.dtype)
         k_rot = torch.empty(b, s, hk, d, device=qg.device, dtype=qg.dtype)
-        c.head_norm_rope(qg, hq, hq * d2, d2, s, q_norm_w, float(eps), cs, sn, int(rotary_dim), q_rot)
-        c.head_norm_rope(k, hk, hk * d, d, s, k_norm_w, float(eps), cs, sn, int(rotary_dim), k_rot)
+        c.head_norm_rope(qg, hq, qg.stride(1), qg.stride(2), s, q_norm_w, float(eps), cs, sn, int(rotary_dim), q_rot)
+        c.head_norm_rope(k, hk, k.stride(1), k.stride(2), s, k_norm_w, float(eps), cs, sn, int(rotary_dim), k_rot)
         out = torch.empty(b, s, hq, d, device=qg.device, dtype=qg.dtype)
-        gate = qg[..., d:]
-        c.vattn_fwd(q_rot, k_rot, v, gate, hq * d2, d2, out)
+        c.vattn_fwd(q_rot, k_rot, v, qg[..., d:], qg.stride(1), qg.stride(2), out)
         return out
     q, gate = qg[..., :d], qg[..., d:]
     q = qwen_norm(q, q_norm_w, eps)
     k = qwen_norm(k, k_norm_w, eps)
     return causal_attention_gated(q, k, v, gate, cos, sin, rotary_dim)
+
+
+# ---------------------------------------------------------------------------- fused producers (CUDA)
+def quantize(x):
+    """1 x 128 dynamic e4m3 quantisation of bf16 rows: (codes uint8 [T, K], scales fp32 [T, K/128])."""
+    t, k = x.shape
+    q = torch.empty(t, k, device=x.device, dtype=torch.uint8)
+    s = torch.empty(t, k // 128, device=x.device, dtype=torch.float32)
+    _c().quant_e4m3(x.contiguous(), q, s)
+    return q, s
+
+
+def fp8_gemm(q, s, w, scale_inv):
+    """bf16 [T, N] = block-scaled GEMM of pre-quantised activations (``quantize``) and e4m3 weights."""
+    out = torch.empty(q.shape[0], w.shape[0], device=q.device, dtype=torch.bfloat16)
+    _c().fp8_gemm(q, s, w, scale_inv, out)
+    return out
+
+
+def add_norm(x, y, w, eps, *, want_bf16=True, want_q=False):
+    """x' = x + y (y may be None), n = (1+w)-RMSNorm(x'); returns (x', n bf16 or None,
+    (codes, scales) or None). One kernel; the quantised form feeds ``fp8_gemm``."""
+    h = x.shape[-1]
+    rows = x.numel() // h
+    x2 = x.reshape(rows, h)
+    xo = torch.empty_like(x2) if y is not None else None
+    n = torch.empty_like(x2) if want_bf16 else None
+    q = torch.empty(rows, h, device=x.device, dtype=torch.uint8) if want_q else None
+    sc = torch.empty(rows, h // 128, device=x.device, dtype=torch.float32) if want_q else None
+    _c().add_norm(x2, None if y is None else y.reshape(rows, h), w, float(eps), xo, n, q, sc)
+    xo = x if xo is None else xo.view(x.shape)
+    return xo, (None if n is None else n.view(x.shape)), ((q, sc) if want_q else None)
+
+
+def silu_mul_quantize(gu):
+    """[T, 2m] fused gate|up projection -> e4m3 codes and scales of bf16(silu(gate) * up)."""
+    t, m2 = gu.shape
+    m = m2 // 2
+    q = torch.empty(t, m, device=gu.device, dtype=torch.uint8)
+    s = torch.empty(t, m // 128, device=gu.device, dtype=torch.float32)
+    _c().silu_mul_quant(gu, q, s)
+    return q, s
+
+
+def gated_norm_quantize(o, z, nv, z_row_stride, w, eps):
+    """o [T * nv, 128] with gates z (token rows of ``z_row_stride``) -> e4m3 codes and scales."""
+    rows = o.shape[0]
+    q = torch.empty(rows, 128, device=o.device, dtype=torch.uint8)
+    s = torch.empty(rows, 1, device=o.device, dtype=torch.float32)
+    _c().gated_norm_quant(o, z, int(nv), int(z_row_stride), w, float(eps), q, s)
+    return q, s
+
+
+def causal_conv_silu_rows(x, ld, w, channels):
+    """Causal depthwise conv + SiLU over the first ``channels`` of token rows of stride ``ld``."""
+    b, s = x.shape[0], x.shape[1]
+    y = torch.empty(b, s, channels, device=x.device, dtype=x.dtype)
+    _c().conv_silu_vec(x, int(ld), w.reshape(w.shape[0], -1).contiguous(), y)
+    return y
 
 
 def gated_delta_rule_backward(q, k, v, g, beta, dout, groups=1):

@@ -96,16 +96,46 @@ def test_truncated_rank_file_is_refused(saved):
 
 
 def test_mismatched_dtype_objective_or_config_is_refused(saved):
-    with pytest.raises(ValueError):
+    with pytest.raises(checkpoint.CheckpointMismatch, match="dtype: checkpoint 'torch.float32', run 'torch.bfloat16'"):
         _restore(saved, dtype=torch.bfloat16)
-    with pytest.raises(ValueError, match="objective"):
+    with pytest.raises(checkpoint.CheckpointMismatch, match="objective.num_anchors: checkpoint 4, run 5"):
         _restore(saved, objective=N.Objective(num_anchors=5))
     meta_path = os.path.join(saved, "metadata.json")
     meta = json.load(open(meta_path))
     meta["config"]["hidden_size"] += 1
+    meta["target_revision"] = "other"
     json.dump(meta, open(meta_path, "w"))
-    with pytest.raises(ValueError, match="configuration"):
+    with pytest.raises(ValueError) as e:  # every mismatched field is listed
         _restore(saved)
+    assert "config.hidden_size: checkpoint 65, run 64" in str(e.value)
+    assert "target_revision: checkpoint 'other'" in str(e.value)
+
+
+def test_async_and_periodic_saves_roundtrip():
+    c, m = _model()
+    opt = N.AdamW(m.sharding, lr=1e-3)
+    o = N.Objective(num_anchors=4)
+    with tempfile.TemporaryDirectory() as d:
+        prefix = os.path.join(d, "run")
+        per = checkpoint.Periodic(prefix, m, opt, o, every=2, keep=2)
+        masters = {}
+        for step in range(1, 7):
+            r = _step(c, m, opt)
+            assert bool(r.update["updated"])
+            per.step(step)
+            masters[step] = [s.master.clone() for s in m.sharding]
+        per.close()
+        import glob
+        gens = sorted(glob.glob(prefix + "-step*"))
+        assert len(gens) == 2  # steps 4 and 6 kept, step 2 pruned
+        newest = checkpoint.latest(prefix)
+        assert json.load(open(os.path.join(newest, "metadata.json")))["step"] == 6
+        c2, m2 = _model()
+        opt2 = N.AdamW(m2.sharding, lr=1e-3)
+        assert checkpoint.restore(newest, m2, opt2, o) == 6
+        assert opt2.steps == opt.steps
+        for a, b in zip(m2.sharding, masters[6]):
+            assert torch.equal(a.master, b)
 
 
 # ---------------------------------------------------------------------------- a rank dies

@@ -168,3 +168,27 @@ def test_gated_attention_large_logits_rescale():
     expect = o * qg[..., D:].sigmoid()
     got = vops.gated_attention(qg.cuda(), k.cuda(), v.cuda(), w.cuda(), w.cuda(), 1e-6, cos.cuda(), sin.cuda(), rd)
     close(got, expect, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+def test_fused_stage_matches_cpu(tmp_path):
+    """The CUDA fused path (concatenated projections, residual add fused with the next
+    norm, producers that emit e4m3 + scales, tcgen05 attention, chunked GDN) against
+    the CPU statement path on a small config with the 27B head geometry (d_v = 128,
+    attention head_dim 128, FP8 projections)."""
+    from nanospec_b200.models.verifier import (Checkpoint, QwenStage, stage_forward, tiny_hybrid_text_config,
+                                               write_synthetic_checkpoint)
+    tc = tiny_hybrid_text_config(hidden=256, vocab=512, heads=2, head_dim=128, ffn=512)
+    tc.update(linear_num_key_heads=1, linear_num_value_heads=2, linear_key_head_dim=128, linear_value_head_dim=128,
+              num_key_value_heads=1)
+    path = write_synthetic_checkpoint(tmp_path / "ckpt", tc, seed=3, fp8=True)
+    ck = Checkpoint(path)
+    ids = torch.randint(0, 512, (2, 200))
+    outs = {}
+    for dev in ("cpu", "cuda"):
+        st = QwenStage(ck, 0, 4, device=dev, first=True, last=True)
+        assert st.fused == (dev == "cuda")
+        outs[dev] = stage_forward(st, ids.to(dev), capture=(0, 1, 2, 3))
+    close(outs["cuda"][0], outs["cpu"][0], rtol=5e-2, cos_min=0.995)
+    for i in (0, 1, 2, 3):
+        close(outs["cuda"][1][i], outs["cpu"][1][i], rtol=5e-2, cos_min=0.995)
