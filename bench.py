@@ -435,6 +435,9 @@ def main():
     if args.impl == "ours":
         from nanospec_b200.ops._ext import cuda_ops
         cuda_ops()  # fail loudly if the extension is missing
+    if world > 1 and rank == 0:
+        from nanospec_b200.utils.provenance import preflight
+        preflight(world)  # GPU count, all-to-all peer access, NVLink (raises otherwise)
     wl = (FullWorkload if full else DraftWorkload)(args, args.impl, world, rank, dev)
     inputs = wl.inputs
 
@@ -555,11 +558,26 @@ def main():
         }
         if args.impl == "reference":
             out["impl"] = "reference"
+        out["provenance"] = _provenance(world)
         print(json.dumps(out), flush=True)
     wl.close(world)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _provenance(world):
+    """Compact provenance for the JSON line: devices, versions, git head, one sha256
+    over every product source file, and the link types between the GPUs."""
+    import re
+
+    from nanospec_b200.utils.provenance import provenance
+    p = provenance(world)
+    links = sorted(set(re.findall(r"\bNV\d+\b", p.pop("topology", ""))))
+    p.pop("source_files", None)
+    p.pop("peer_access", None)
+    p["links"] = links
+    return p
 
 
 def _print_unavailable(n, why, args):

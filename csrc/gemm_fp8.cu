@@ -10,8 +10,8 @@
 // epilogue warps promote it: acc += sa * sb * partial, in fp32 registers, while the
 // tensor cores already work on the next K block.
 //
-// CTA: 128 tokens x 128 output channels. warp 0: TMA producer; warp 1: TMEM owner +
-// MMA issuer; warps 2-5: promotion/epilogue (TMEM lane quarter = warp % 4).
+// Tiles of 128 tokens x 256 output channels (128 when N is not a multiple of 256), one
+// persistent CTA per SM; see fp8_gemm_kernel below for the warp roles.
 #include "common.h"
 #include "sm100.cuh"
 
@@ -19,10 +19,17 @@
 
 namespace ns {
 
-constexpr int F8_BM = 128, F8_BN = 128, F8_BK = 128;
-constexpr int F8_STAGE = F8_BM * F8_BK + F8_BN * F8_BK;  // bytes
-constexpr int F8_STAGES = 6;
-constexpr int F8_SMEM = F8_STAGES * F8_STAGE + 1024 + 512;
+constexpr int F8_BM = 128, F8_BK = 128;
+
+template <int BN>
+struct F8Cfg {
+  static constexpr int STAGE = F8_BM * F8_BK + BN * F8_BK;  // bytes
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 512;
+  static constexpr int PWARPS = BN / 32;                    // promotion warps: 128 columns each per quarter
+  static constexpr int THREADS = 64 + 32 * PWARPS;
+  static constexpr int TMEM_COLS = 2 * BN;                  // two partial buffers
+};
 
 // kind::f8f6f4 instruction descriptor: e4m3 x e4m3 -> f32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
@@ -47,37 +54,47 @@ struct F8Args {
   int* err;
 };
 
-__global__ void __launch_bounds__(192, 1)
+// Persistent: CTA c walks tiles c, c + grid, ... (m-tile fastest, so CTAs running at
+// the same time share weight tiles in L2). The smem ring, the two TMEM partial
+// buffers and every barrier phase continue across tile boundaries (a global K-block
+// counter `it`), so the next tile's MMAs start while this tile's last partial is
+// promoted and stored. Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2.. the
+// promotion warps (BN / 32 of them; warp w owns TMEM lane quarter w % 4 and the
+// 128-column half (w - 2) / 4 of the tile, whose weight scale is one block).
+template <int BN>
+__global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, F8Args args) {
+  using C = F8Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + F8_STAGES * F8_BM * F8_BK;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + F8_STAGES * F8_BN * F8_BK);
-  uint64_t* empty = full + F8_STAGES;
-  uint64_t* tfull = empty + F8_STAGES;  // [2] accumulator buffer ready
-  uint64_t* tempty = tfull + 2;         // [2] accumulator buffer drained
+  uint8_t* sB = smem + C::STAGES * F8_BM * F8_BK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * BN * F8_BK);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;  // [2] partial buffer ready
+  uint64_t* tempty = tfull + 2;         // [2] partial buffer drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * F8_BM, n0 = blockIdx.y * F8_BN;
   const int nkb = (args.K + F8_BK - 1) / F8_BK;
+  const int mt = (args.M + F8_BM - 1) / F8_BM, nt = args.N / BN;
+  const int tiles = mt * nt;
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < F8_STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&tfull[b], 1);
-      sm100::mbar_init(&tempty[b], 128);
+      sm100::mbar_init(&tempty[b], 32 * C::PWARPS);
     }
     sm100::fence_barrier_init();
     sm100::tma_prefetch_desc(&ta);
     sm100::tma_prefetch_desc(&tb);
   }
   if (warp == 1) {
-    sm100::tmem_alloc(tmem_slot, 256);
+    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
@@ -87,84 +104,94 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % F8_STAGES;
-        const uint32_t ph = (i / F8_STAGES) & 1;
-        if (i >= F8_STAGES && !sm100::mbar_wait(&empty[s], ph ^ 1, args.err)) break;
-        sm100::mbar_expect_tx(&full[s], F8_STAGE);
-        sm100::tma_load_2d(sA + s * F8_BM * F8_BK, &ta, &full[s], i * F8_BK, m0);
-        sm100::tma_load_2d(sB + s * F8_BN * F8_BK, &tb, &full[s], i * F8_BK, n0);
-        issued = i + 1;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile % mt) * F8_BM, n0 = (tile / mt) * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          if (it >= C::STAGES && !sm100::mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, args.err)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_expect_tx(&full[s], C::STAGE);
+          sm100::tma_load_2d(sA + s * F8_BM * F8_BK, &ta, &full[s], kb * F8_BK, m0);
+          sm100::tma_load_2d(sB + s * BN * F8_BK, &tb, &full[s], kb * F8_BK, n0);
+        }
       }
-      for (int i = max(0, issued - F8_STAGES); i < issued; ++i)
-        sm100::mbar_wait(&full[i % F8_STAGES], (i / F8_STAGES) & 1, args.err);
+      // drain: the last loads of every stage have landed before the CTA exits
+      for (int i = max(0, it - C::STAGES); i < it; ++i)
+        sm100::mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, args.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3(F8_BM, F8_BN);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % F8_STAGES;
-        const uint32_t ph = (i / F8_STAGES) & 1;
-        const int buf = i & 1;
-        // accumulator buffer `buf` must have been drained by the promotion warps
-        if (i >= 2 && !sm100::mbar_wait(&tempty[buf], ((i >> 1) - 1) & 1, args.err)) break;
-        if (!sm100::mbar_wait(&full[s], ph, args.err)) break;
-        sm100::tc_fence_after();
-        const uint32_t a_base = sm100::smem_u32(sA + s * F8_BM * F8_BK);
-        const uint32_t b_base = sm100::smem_u32(sB + s * F8_BN * F8_BK);
-        const uint32_t d = tmem + (uint32_t)(buf * F8_BN);
+      constexpr uint32_t idesc = idesc_e4m3(F8_BM, BN);
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const int buf = it & 1;
+          if (it >= 2 && !sm100::mbar_wait(&tempty[buf], ((it >> 1) - 1) & 1, args.err)) { ok = false; break; }
+          if (!sm100::mbar_wait(&full[s], (it / C::STAGES) & 1, args.err)) { ok = false; break; }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_u32(sA + s * F8_BM * F8_BK);
+          const uint32_t b_base = sm100::smem_u32(sB + s * BN * F8_BK);
+          const uint32_t d = tmem + (uint32_t)(buf * BN);
 #pragma unroll
-        for (int kk = 0; kk < F8_BK / 32; ++kk) {
-          const uint64_t ad = sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
-          const uint64_t bd = sm100::smem_desc_sw128(b_base + kk * 32, 0, 1024);
-          mma_f8(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < F8_BK / 32; ++kk) {
+            const uint64_t ad = sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
+            const uint64_t bd = sm100::smem_desc_sw128(b_base + kk * 32, 0, 1024);
+            mma_f8(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          sm100::mma_commit(&empty[s]);
+          sm100::mma_commit(&tfull[buf]);
         }
-        sm100::mma_commit(&empty[s]);
-        sm100::mma_commit(&tfull[buf]);
       }
     }
   } else {
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const int m = m0 + row;
     const int kbs = (args.K + 127) / 128;
-    float acc[F8_BN];
-#pragma unroll
-    for (int j = 0; j < F8_BN; ++j) acc[j] = 0.f;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int it = 0;
     bool ok = true;
-    for (int i = 0; i < nkb && ok; ++i) {
-      const int buf = i & 1;
-      ok = sm100::mbar_wait(&tfull[buf], (i >> 1) & 1, args.err);
-      if (!ok) break;
-      sm100::tc_fence_after();
-      const float sbv = args.sb[(n0 / 128) * kbs + i];
-      const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + i] : 0.f;
-      const float f = sav * sbv;
+    for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      const int m0 = (tile % mt) * F8_BM, n0 = (tile / mt) * BN;
+      const int m = m0 + row;
+      const int nb = n0 / 128 + half;
+      float acc[128];
 #pragma unroll
-      for (int c = 0; c < F8_BN; c += 32) {
-        float v[32];
-        sm100::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * F8_BN + c), v);
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int buf = it & 1;
+        ok = sm100::mbar_wait(&tfull[buf], (it >> 1) & 1, args.err);
+        if (!ok) break;
+        sm100::tc_fence_after();
+        const float sbv = args.sb[nb * kbs + kb];
+        const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + kb] : 0.f;
+        const float f = sav * sbv;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c + j] += f * v[j];
+        for (int c = 0; c < 128; c += 32) {
+          float v[32];
+          sm100::tmem_ld32(tmem + lane_off + (uint32_t)(buf * BN + half * 128 + c), v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c + j] = fmaf(f, v[j], acc[c + j]);
+        }
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&tempty[buf]);
       }
-      sm100::tc_fence_before();
-      sm100::mbar_arrive(&tempty[buf]);
-    }
-    if (ok && m < args.M) {
-      __nv_bfloat16* o = args.out + (int64_t)m * args.ldo + n0;
-      if (n0 + F8_BN <= args.N && (args.ldo % 8) == 0) {
+      if (ok && m < args.M) {
+        __nv_bfloat16* o = args.out + (int64_t)m * args.ldo + n0 + half * 128;
         uint4* p = reinterpret_cast<uint4*>(o);
 #pragma unroll
-        for (int j = 0; j < F8_BN / 8; ++j) {
+        for (int j = 0; j < 16; ++j) {
           __nv_bfloat162 h[4];
 #pragma unroll
           for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[8 * j + 2 * t], acc[8 * j + 2 * t + 1]);
           p[j] = *reinterpret_cast<uint4*>(h);
         }
-      } else {
-        for (int j = 0; j < F8_BN; ++j)
-          if (n0 + j < args.N) o[j] = __float2bfloat16(acc[j]);
       }
     }
   }
@@ -172,7 +199,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, 256);
+    sm100::tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -237,8 +264,8 @@ void fp8_gemm(at::Tensor q, at::Tensor sa, at::Tensor w, at::Tensor scale_inv, a
            "weight_scale_inv must be fp32 [N/128, K/128]");
   NS_CHECK(sa.scalar_type() == at::kFloat && sa.size(0) == T && sa.size(1) == K / 128, "sa must be fp32 [T, K/128]");
   if (T == 0) return;
-  CUtensorMap ta = make_tmap_u8(q.data_ptr(), T, K, F8_BM);
-  CUtensorMap tb = make_tmap_u8(w.data_ptr(), N, K, F8_BN);
+  NS_CHECK((out.stride(0) % 8) == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "fp8_gemm: output rows must be 16-byte aligned");
   F8Args a{};
   a.M = (int)T;
   a.N = N;
@@ -248,12 +275,27 @@ void fp8_gemm(at::Tensor q, at::Tensor sa, at::Tensor w, at::Tensor scale_inv, a
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = out.stride(0);
   a.err = device_error_flag();
-  static std::atomic<unsigned long long> attr{0};
-  once_per_device(attr, [&] {
-    NS_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F8_SMEM));
-  });
-  dim3 grid((unsigned)((T + F8_BM - 1) / F8_BM), (unsigned)(N / F8_BN));
-  fp8_gemm_kernel<<<grid, 192, F8_SMEM, stream()>>>(ta, tb, a);
+  CUtensorMap ta = make_tmap_u8(q.data_ptr(), T, K, F8_BM);
+  const int mt = (int)((T + F8_BM - 1) / F8_BM);
+  if (N % 256 == 0) {
+    using C = F8Cfg<256>;
+    CUtensorMap tb = make_tmap_u8(w.data_ptr(), N, K, 256);
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [&] {
+      NS_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    });
+    const int grid = std::min(mt * (N / 256), num_sms());
+    fp8_gemm_kernel<256><<<grid, C::THREADS, C::SMEM, stream()>>>(ta, tb, a);
+  } else {
+    using C = F8Cfg<128>;
+    CUtensorMap tb = make_tmap_u8(w.data_ptr(), N, K, 128);
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [&] {
+      NS_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    });
+    const int grid = std::min(mt * (N / 128), num_sms());
+    fp8_gemm_kernel<128><<<grid, C::THREADS, C::SMEM, stream()>>>(ta, tb, a);
+  }
   NS_CUDA(cudaGetLastError());
 }
 

@@ -118,6 +118,9 @@ def main(argv=None):
     world = int(os.environ.get("WORLD_SIZE", 1))
     topo = Topology(world=world, train_gpus=args.train_gpus)
     node = Node(args.train_gpus, topology=topo, backend=args.backend)
+    if node.backend == "nccl" and world > 1 and node.rank == 0:
+        from .utils.provenance import preflight
+        preflight(world)  # GPU count, all-to-all peer access, NVLink (raises otherwise)
     torch.set_float32_matmul_precision("highest")
     c = DraftConfig.load(config_path(args.config))
     o = Objective(num_anchors=args.anchors)
@@ -209,6 +212,7 @@ def main(argv=None):
                 "target_revision": TARGET_REVISION, "train_gpus": args.train_gpus, "world": world,
                 "dtype": args.dtype, "learning_rate": opt.lr, "steps": rows, "checkpoint": ckpt_path,
                 "verifier": bool(teacher is not None),
+                "provenance": _provenance(node, world),
             }, indent=2))
     if model is not None and world > 1:
         model.sharding.close_peer()
@@ -216,6 +220,13 @@ def main(argv=None):
         dist.barrier()
         dist.destroy_process_group()
     return rows
+
+
+def _provenance(node, world):
+    from .utils.provenance import provenance, source_hashes
+    if node.backend == "nccl":
+        return provenance(world)
+    return {"source_files": source_hashes(), "torch": torch.__version__}
 
 
 if __name__ == "__main__":

@@ -189,7 +189,8 @@ def bench_verifier(a):
                    config=synthetic_hf_config(tc))
     ids = torch.randint(0, tc["vocab_size"], (1, a.S), device="cuda")
     names = ("embedding", "add", "silu_mul", "qwen_norm", "qwen_gated_norm", "fp8_linear", "causal_conv_silu",
-             "gdn_gates", "gated_delta_rule", "causal_attention_gated", "gated_attention")
+             "gdn_gates", "gated_delta_rule", "causal_attention_gated", "gated_attention", "fp8_gemm", "quantize",
+             "add_norm", "silu_mul_quantize", "gated_norm_quantize", "causal_conv_silu_rows")
     times, orig = {}, {n: getattr(vops, n) for n in names}
 
     def wrap(name, fn):
@@ -215,8 +216,9 @@ def bench_verifier(a):
         for n in names:
             setattr(vops, n, orig[n])
     per = {n: round(sum(e0.elapsed_time(e1) for e0, e1 in v) / a.reps, 3) for n, v in times.items()}
+    gemm_ms = per.get("fp8_gemm", 0.0) + per.get("fp8_linear", 0.0)
     return {"op": "verifier_4_layers", "S": a.S, "stage_ms": round(whole, 3), "op_ms": per,
-            "fp8_tflops": round(_verifier_fp8_flops(tc, a.S) / (per.get("fp8_linear", 1e9) * 1e9), 1)}
+            "fp8_tflops": round(_verifier_fp8_flops(tc, a.S) / (gemm_ms * 1e9), 1) if gemm_ms else None}
 
 
 def _verifier_fp8_flops(tc, s):

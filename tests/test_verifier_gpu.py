@@ -30,7 +30,8 @@ def _check():
 
 
 @cuda
-@pytest.mark.parametrize("T,K,N", [(200, 512, 384), (16, 256, 128), (1000, 1024, 640)])
+@pytest.mark.parametrize("T,K,N", [(200, 512, 384), (16, 256, 128), (1000, 1024, 640), (300, 512, 768),
+                                   (128, 256, 512), (1100, 1024, 2560)])
 def test_fp8_linear(T, K, N):
     from nanospec_b200.models.verifier import quantize_weight_blocks
     x = torch.randn(T, K).bfloat16()
@@ -189,6 +190,23 @@ def test_fused_stage_matches_cpu(tmp_path):
         st = QwenStage(ck, 0, 4, device=dev, first=True, last=True)
         assert st.fused == (dev == "cuda")
         outs[dev] = stage_forward(st, ids.to(dev), capture=(0, 1, 2, 3))
-    close(outs["cuda"][0], outs["cpu"][0], rtol=5e-2, cos_min=0.995)
-    for i in (0, 1, 2, 3):
-        close(outs["cuda"][1][i], outs["cpu"][1][i], rtol=5e-2, cos_min=0.995)
+    # The fused CUDA path against the CUDA statement path: the same mixer kernels, so
+    # only the fusion (concatenated GEMMs, add+norm, quantising producers) differs and
+    # only through roundings inside fp32 reductions (a 1-ulp bf16 flip of a norm output
+    # can move an e4m3 code). With random weights such differences grow by a few times
+    # per layer, so the criterion is relative L2 and cosine, not the largest element.
+    st = QwenStage(ck, 0, 4, device="cuda", first=True, last=True)
+    st.fused = False
+    plain = stage_forward(st, ids.cuda(), capture=(0, 1, 2, 3))
+    for got, ref_ in [(outs["cuda"][1][i], plain[1][i]) for i in range(4)] + [(outs["cuda"][0], plain[0])]:
+        rel_close(got, ref_, rel=3e-2, cos_min=0.9995)
+    # against the CPU statements (bf16 attention scores, fp32 dequantised GEMMs, fp32 GDN)
+    for got, ref_ in [(outs["cuda"][1][i], outs["cpu"][1][i]) for i in range(4)] + [(outs["cuda"][0], outs["cpu"][0])]:
+        rel_close(got, ref_, rel=1e-1, cos_min=0.995)
+
+
+def rel_close(a, b, rel, cos_min):
+    a, b = a.float().cpu(), b.float().cpu()
+    r = ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+    cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+    assert r <= rel and cos >= cos_min, f"relative L2 {r:.3e}, cos {cos:.6f}"
