@@ -11,13 +11,13 @@
 //
 // The chunk-local part is independent across chunks, so it runs as its own kernel
 // over every (chunk, head, row) at once (`gdn_prep_kernel`: 3072 CTAs at 48 heads x
-// 4096 tokens). Only the state recurrence is sequential; it is split across value
-// columns (columns of S are independent), so `gdn_state_kernel` runs
-// (d_v / 32) x heads x rows CTAs, two per SM, each walking the chunks with its slice
-// of S in shared memory. The prep kernel hands over, per chunk and head, W^T, U
-// (slice-major), A^T, (q e^G)^T, k e^{G_last - G} and e^{G_last}; the state kernel
-// fetches them with bulk copies (cp.async.bulk, this GPU's memory only) completing on
-// an mbarrier with a bounded wait.
+// 4096 tokens). Only the state recurrence is sequential. At d = 128 (the 27B shape)
+// it runs on tcgen05 (`gdn_state_tc_kernel`: one CTA per head, the fp32 state in
+// TMEM, four MMAs per chunk, operand tiles by TMA). Other head sizes use
+// `gdn_state_kernel` on CUDA cores, split across value columns (columns of S are
+// independent): (d_v / 32) x heads x rows CTAs, two per SM, each walking the chunks
+// with its slice of S in shared memory, fed by bulk copies (cp.async.bulk, this
+// GPU's memory only) completing on an mbarrier with a bounded wait.
 //
 // The triangular inverse is blocked: 16 x 16 diagonal blocks by column-parallel
 // forward substitution (each thread owns one column, no barriers), then the three
@@ -56,13 +56,19 @@ struct Prep {
   static constexpr int BYTES = FLOATS * 4;
 };
 
-template <int D>
+// Outputs per (row, head, chunk) ck, two layouts:
+//  TC = false (CUDA-core state kernel): WT fp32 [D][C], QgT bf16 [D][C], Kd bf16 [C][D],
+//      AqkT fp32 [C][C] (A transposed), U fp32 slice-major [D/dvs][C][dvs];
+//  TC = true (tensor-core state kernel, operands K-major for tcgen05): W bf16 [C][D],
+//      Qg bf16 [C][D], Kd^T bf16 [D][C], A bf16 [C][C], U^T fp32 [D][C].
+// GL fp32 = e^{G_last} either way.
+template <int D, bool TC>
 __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                       const bf16* __restrict__ v, const float* __restrict__ gin,
                                                       const bf16* __restrict__ beta_in, int s, int nk, int nv,
-                                                      int groups, int nchunks, float* __restrict__ WT,
-                                                      bf16* __restrict__ QgT, bf16* __restrict__ Kd,
-                                                      float* __restrict__ AqkT, float* __restrict__ Uo,
+                                                      int groups, int nchunks, void* __restrict__ Wo,
+                                                      bf16* __restrict__ QgO, bf16* __restrict__ KdO,
+                                                      void* __restrict__ AqkO, float* __restrict__ Uo,
                                                       float* __restrict__ GL, int dvs) {
   using L = Prep<D>;
   constexpr int DP = L::DP;
@@ -135,14 +141,24 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
 
   // 2. M = strict_lower(beta_i k_i.k_j e^{G_i-G_j}) and A = lower(scale q_i.k_j e^{G_i-G_j});
   //    each thread a 4 x 4 block of both. A goes to global memory transposed.
+  // Only the 136 blocks on or below the diagonal exist: thread t < 136 takes block
+  // (bi, bj) of the triangle, so no lane of a working warp idles through the loop;
+  // the blocks above the diagonal are zero and written by the remaining threads.
   {
-    const int i0 = (tid >> 4) * 4, j0 = (tid & 15) * 4;
-    float kk[4][4], qk[4][4];
+    constexpr int NB = C / 4, TRI = NB * (NB + 1) / 2;
+    float* at = reinterpret_cast<float*>(AqkO) + ck * C * C;   // TC = false: A^T fp32
+    bf16* ab = reinterpret_cast<bf16*>(AqkO) + ck * C * C;     // TC = true: A bf16 row-major
+    if (tid < TRI) {
+      int bi2 = (int)((sqrtf(8.f * tid + 1.f) - 1.f) * 0.5f);
+      if ((bi2 + 1) * (bi2 + 2) / 2 <= tid) ++bi2;
+      if (bi2 * (bi2 + 1) / 2 > tid) --bi2;
+      const int bj = tid - bi2 * (bi2 + 1) / 2;
+      const int i0 = bi2 * 4, j0 = bj * 4;
+      float kk[4][4], qk[4][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) kk[r][c] = qk[r][c] = 0.f;
-    if (j0 <= i0 + 3) {
+        for (int c = 0; c < 4; ++c) kk[r][c] = qk[r][c] = 0.f;
 #pragma unroll 4
       for (int d = 0; d < D; ++d) {
         const float4 ki = *reinterpret_cast<const float4*>(&kT[d * CP + i0]);
@@ -158,34 +174,78 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
             qk[r][c] = fmaf(qiv[r], kjv[c], qk[r][c]);
           }
       }
-    }
-    float* at = AqkT + ck * C * C;
+      float a16[4][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int j = j0 + c;
-      float a4[4];
+      for (int c = 0; c < 4; ++c) {
+        const int j = j0 + c;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int i = i0 + r;
-        const float dec = j <= i ? expf(G[i] - G[j]) : 0.f;
-        Ms[i * (C + 1) + j] = j < i ? Bt[i] * kk[r][c] * dec : 0.f;
-        a4[r] = j <= i ? scale * qk[r][c] * dec : 0.f;
+        for (int r = 0; r < 4; ++r) {
+          const int i = i0 + r;
+          const float dec = j <= i ? expf(G[i] - G[j]) : 0.f;
+          Ms[i * (C + 1) + j] = j < i ? Bt[i] * kk[r][c] * dec : 0.f;
+          a16[r][c] = j <= i ? scale * qk[r][c] * dec : 0.f;
+        }
       }
-      *reinterpret_cast<float4*>(&at[j * C + i0]) = make_float4(a4[0], a4[1], a4[2], a4[3]);
+      if constexpr (TC) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(a16[r][0], a16[r][1]);
+          __nv_bfloat162 hi = __floats2bfloat162_rn(a16[r][2], a16[r][3]);
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t*>(&lo);
+          pk.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(&ab[(i0 + r) * C + j0]) = pk;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<float4*>(&at[(j0 + c) * C + i0]) =
+              make_float4(a16[0][c], a16[1][c], a16[2][c], a16[3][c]);
+      }
+    } else {
+      // zero blocks above the diagonal: (row block i, column block j), j > i
+      for (int idx = tid - TRI; idx < NB * NB - TRI; idx += NT - TRI) {
+        int i = 0, rem = idx;
+        while (rem >= NB - 1 - i) {
+          rem -= NB - 1 - i;
+          ++i;
+        }
+        const int j = i + 1 + rem;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) Ms[(i * 4 + r) * (C + 1) + j * 4 + c] = 0.f;
+          if constexpr (TC)
+            *reinterpret_cast<uint2*>(&ab[(i * 4 + c) * C + j * 4]) = make_uint2(0u, 0u);
+          else
+            *reinterpret_cast<float4*>(&at[(j * 4 + c) * C + i * 4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
     }
   }
   __syncthreads();
-  // (q scale e^G)^T and k e^{G_last - G} for the state kernel (bf16)
+  // q scale e^G and k e^{G_last - G} for the state kernel (bf16)
   {
-    bf16* qg = QgT + ck * D * C;
-    bf16* kd = Kd + ck * C * D;
-    for (int idx = tid; idx < D * C; idx += NT) {
-      const int d = idx / C, i = idx % C;
-      qg[idx] = __float2bfloat16(qT[d * CP + i] * scale * eG[i]);
-    }
-    for (int idx = tid; idx < C * D; idx += NT) {
-      const int i = idx / D, d = idx % D;
-      kd[idx] = __float2bfloat16(kT[d * CP + i] * eGl[i]);
+    bf16* qg = QgO + ck * D * C;
+    bf16* kd = KdO + ck * C * D;
+    if constexpr (TC) {
+      for (int idx = tid; idx < C * D; idx += NT) {  // Qg [C][D]
+        const int i = idx / D, d = idx % D;
+        qg[idx] = __float2bfloat16(qT[d * CP + i] * scale * eG[i]);
+      }
+      for (int idx = tid; idx < D * C; idx += NT) {  // Kd^T [D][C]
+        const int d = idx / C, i = idx % C;
+        kd[idx] = __float2bfloat16(kT[d * CP + i] * eGl[i]);
+      }
+    } else {
+      for (int idx = tid; idx < D * C; idx += NT) {  // Qg^T [D][C]
+        const int d = idx / C, i = idx % C;
+        qg[idx] = __float2bfloat16(qT[d * CP + i] * scale * eG[i]);
+      }
+      for (int idx = tid; idx < C * D; idx += NT) {  // Kd [C][D]
+        const int i = idx / D, d = idx % D;
+        kd[idx] = __float2bfloat16(kT[d * CP + i] * eGl[i]);
+      }
     }
     if (tid == 0) GL[ck] = expf(Gl);
   }
@@ -263,16 +323,51 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
         u[r][3] = fmaf(t, xv.w, u[r][3]);
       }
     }
-    float* wt = WT + ck * D * C;
+    if constexpr (TC) {
+      // W bf16 [C][D] straight from registers; U^T fp32 [D][C] through shared memory
+      bf16* wo = reinterpret_cast<bf16*>(Wo) + ck * C * D;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+      for (int r = 0; r < RPT; ++r) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(w[r][0], w[r][1]);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(w[r][2], w[r][3]);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(&wo[(i0 + r) * D + e0]) = pk;
+      }
+      __syncthreads();
+      float* uts = qT;  // [D][CP]
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) wt[(e0 + c) * C + i0 + r] = w[r][c];
-    const int slice = e0 / dvs, el = e0 % dvs;
-    float* uo = Uo + (ck * (D / dvs) + slice) * C * dvs;
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-    for (int r = 0; r < RPT; ++r)
-      *reinterpret_cast<float4*>(&uo[(i0 + r) * dvs + el]) = make_float4(u[r][0], u[r][1], u[r][2], u[r][3]);
+        for (int r = 0; r < RPT; ++r) uts[(e0 + c) * CP + i0 + r] = u[r][c];
+      __syncthreads();
+      float* ut = Uo + ck * D * C;
+      for (int idx = tid; idx < D * C / 4; idx += NT) {
+        const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
+        *reinterpret_cast<float4*>(&ut[e * C + i4]) = *reinterpret_cast<const float4*>(&uts[e * CP + i4]);
+      }
+    } else {
+      const int slice = e0 / dvs, el = e0 % dvs;
+      float* uo = Uo + (ck * (D / dvs) + slice) * C * dvs;
+#pragma unroll
+      for (int r = 0; r < RPT; ++r)
+        *reinterpret_cast<float4*>(&uo[(i0 + r) * dvs + el]) = make_float4(u[r][0], u[r][1], u[r][2], u[r][3]);
+      // W^T: transpose through shared memory (the q^T / beta k e^G area is free now),
+      // then write [D][C] rows with coalesced 16-byte stores
+      __syncthreads();
+      float* wts = qT;  // [D][CP]
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int r = 0; r < RPT; ++r) wts[(e0 + c) * CP + i0 + r] = w[r][c];
+      __syncthreads();
+      float* wt = reinterpret_cast<float*>(Wo) + ck * D * C;
+      for (int idx = tid; idx < D * C / 4; idx += NT) {
+        const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
+        *reinterpret_cast<float4*>(&wt[e * C + i4]) = *reinterpret_cast<const float4*>(&wts[e * CP + i4]);
+      }
+    }
   }
 }
 
@@ -410,6 +505,244 @@ __global__ void __launch_bounds__(NT, 2) gdn_state_kernel(const float* __restric
   }
 }
 
+// ------------------------------------------------------------------ tensor-core state kernel
+// One CTA per (head, row), d_k = d_v = 128. The state is held transposed, S^T [d_v, d_k],
+// as an fp32 tcgen05 accumulator in TMEM (lane = value channel). Per chunk:
+//   MMA1  v'^T  = S^T W^T          M=128 (d_v), N=64 (tokens), K=128 (d_k)
+//   MMA2  o^T   = S^T Qg^T         same shape
+//   rows: v^T = U^T - v'^T -> bf16 A operand
+//   MMA3  o^T  += v^T A^T          M=128, N=64, K=64
+//   MMA4  S^T   = e^{G_last} S^T + v^T Kd     M=128, N=128 (d_k), K=64
+// S^T is read back once per chunk: rounded to bf16 as the A operand of MMA1/2 (the
+// fp32 copy stays in TMEM), and scaled by e^{G_last} in place before MMA4 accumulates.
+// Chunk operand tiles (W, Qg, A, Kd^T, all bf16 K-major) arrive by TMA into a 2-stage
+// ring with 128-byte swizzle. Warps: 0 TMA, 1 MMA issuer + TMEM owner, 2-5 rows.
+namespace tcs {
+constexpr int TILE_W = C * 128 * 2;    // [64][128] bf16, two swizzle atoms
+constexpr int TILE_A = C * C * 2;      // [64][64]
+constexpr int TILE_K = 128 * C * 2;    // [128][64]
+constexpr int STAGE = 2 * TILE_W + TILE_A + TILE_K;   // 56 KB
+constexpr int ST_BYTES = 128 * 128 * 2;               // S^T bf16 [128][128], two atoms
+constexpr int VN_BYTES = 128 * C * 2;                 // v^T bf16 [128][64]
+constexpr int SMEM = ST_BYTES + VN_BYTES + 2 * STAGE + 1024 + 256;
+constexpr int S_COL = 0, VN_COL = 128, O_COL = 192, TMEM_COLS = 256;
+}  // namespace tcs
+
+// 8 bf16 from 8 floats
+__device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+__global__ void __launch_bounds__(192, 1)
+    gdn_state_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tq,
+                        const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tk,
+                        const float* __restrict__ Ut, const float* __restrict__ GL, bf16* __restrict__ out, int s,
+                        int nv, int nchunks, int* err) {
+  using namespace tcs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sS = smem;                    // S^T bf16, A operand of MMA1/2
+  uint8_t* sV = sS + ST_BYTES;           // v^T bf16, A operand of MMA3/4
+  uint8_t* ring = sV + VN_BYTES;         // [2][W | Qg | A | Kd^T]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + 2 * STAGE);
+  uint64_t* full = bars;         // [2]
+  uint64_t* empty = bars + 2;    // [2]
+  uint64_t* a_ready = bars + 4;  // S^T operand + scaled TMEM state ready (4 row warps)
+  uint64_t* v_ready = bars + 5;  // v^T operand ready (4 row warps)
+  uint64_t* mm12 = bars + 6;     // MMA1/2 done
+  uint64_t* mm34 = bars + 7;     // MMA3/4 done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, bi = blockIdx.y;
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], 1);
+    }
+    sm100::mbar_init(a_ready, 4);
+    sm100::mbar_init(v_ready, 4);
+    sm100::mbar_init(mm12, 1);
+    sm100::mbar_init(mm34, 1);
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&tw);
+    sm100::tma_prefetch_desc(&tq);
+    sm100::tma_prefetch_desc(&ta);
+    sm100::tma_prefetch_desc(&tk);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int64_t ck0 = ((int64_t)bi * nv + h) * nchunks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int ch = 0; ch < nchunks; ++ch) {
+        const int st = ch & 1;
+        if (ch >= 2 && !sm100::mbar_wait(&empty[st], ((ch >> 1) - 1) & 1, err)) break;
+        uint8_t* d = ring + st * STAGE;
+        const int row = (int)((ck0 + ch) * C);
+        sm100::mbar_expect_tx(&full[st], STAGE);
+        sm100::tma_load_2d(d, &tw, &full[st], 0, row);
+        sm100::tma_load_2d(d + C * 128, &tw, &full[st], 64, row);
+        sm100::tma_load_2d(d + TILE_W, &tq, &full[st], 0, row);
+        sm100::tma_load_2d(d + TILE_W + C * 128, &tq, &full[st], 64, row);
+        sm100::tma_load_2d(d + 2 * TILE_W, &ta, &full[st], 0, row);
+        sm100::tma_load_2d(d + 2 * TILE_W + TILE_A, &tk, &full[st], 0, (int)((ck0 + ch) * 128));
+        issued = ch + 1;
+      }
+      for (int ch = max(0, issued - 2); ch < issued; ++ch) sm100::mbar_wait(&full[ch & 1], (ch >> 1) & 1, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id64 = sm100::idesc_bf16(128, C, false, false);
+      constexpr uint32_t id128 = sm100::idesc_bf16(128, 128, false, false);
+      const uint32_t s_base = sm100::smem_u32(sS), v_base = sm100::smem_u32(sV);
+      for (int ch = 0; ch < nchunks; ++ch) {
+        const int st = ch & 1;
+        if (!sm100::mbar_wait(a_ready, ch & 1, err)) break;
+        if (!sm100::mbar_wait(&full[st], (ch >> 1) & 1, err)) break;
+        sm100::tc_fence_after();
+        const uint32_t r_base = sm100::smem_u32(ring + st * STAGE);
+        const uint32_t w_base = r_base, q_base = r_base + TILE_W, a_base = r_base + 2 * TILE_W,
+                       k_base = a_base + TILE_A;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // K = d_k = 128
+          const uint64_t ad = sm100::smem_desc_sw128(s_base + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 0, 1024);
+          const uint64_t bw = sm100::smem_desc_sw128(w_base + (kk >> 2) * (C * 128) + (kk & 3) * 32, 0, 1024);
+          const uint64_t bq = sm100::smem_desc_sw128(q_base + (kk >> 2) * (C * 128) + (kk & 3) * 32, 0, 1024);
+          sm100::mma_bf16(tmem + VN_COL, ad, bw, id64, kk > 0 ? 1u : 0u);
+          sm100::mma_bf16(tmem + O_COL, ad, bq, id64, kk > 0 ? 1u : 0u);
+        }
+        sm100::mma_commit(mm12);
+        if (!sm100::mbar_wait(v_ready, ch & 1, err)) break;
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {  // K = 64 tokens of the chunk
+          const uint64_t av = sm100::smem_desc_sw128(v_base + kk * 32, 0, 1024);
+          const uint64_t ba = sm100::smem_desc_sw128(a_base + kk * 32, 0, 1024);
+          const uint64_t bk = sm100::smem_desc_sw128(k_base + kk * 32, 0, 1024);
+          sm100::mma_bf16(tmem + O_COL, av, ba, id64, 1u);
+          sm100::mma_bf16(tmem + S_COL, av, bk, id128, (ch > 0 || kk > 0) ? 1u : 0u);
+        }
+        sm100::mma_commit(mm34);
+        sm100::mma_commit(&empty[st]);
+      }
+    }
+  } else {
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // value channel = TMEM lane = A-operand row
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    bool ok = true;
+    for (int ch = 0; ch < nchunks && ok; ++ch) {
+      const int64_t ck = ck0 + ch;
+      // ---- (a) state operand for this chunk
+      if (ch == 0) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          *reinterpret_cast<uint4*>(sS + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        ok = __all_sync(0xffffffff, sm100::mbar_wait(mm34, (ch - 1) & 1, err));
+        if (!ok) break;
+        sm100::tc_fence_after();
+        // previous chunk's output o^T, then S^T -> bf16 operand and e^{G_last} S^T in place
+        {
+          const int t0 = (ch - 1) * C;
+          const int cnt = min(C, s - t0);
+#pragma unroll 1
+          for (int c = 0; c < C; c += 32) {
+            float o[32];
+            sm100::tmem_ld32(tmem + lane_off + O_COL + c, o);
+            for (int i = 0; i < 32 && c + i < cnt; ++i)
+              out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
+          }
+        }
+        const float gl = GL[ck];
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          float v[32];
+          sm100::tmem_ld32(tmem + lane_off + S_COL + c, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int ch16 = (c >> 3) + j;  // 16-byte chunk index along d_k (0..15)
+            *reinterpret_cast<uint4*>(sS + (ch16 >> 3) * (128 * 128) + r * 128 + (((ch16 & 7) ^ (r & 7)) << 4)) =
+                pack_bf16x8(v + 8 * j);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= gl;
+          sm100::tmem_st32(tmem + lane_off + S_COL + c, v);
+        }
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(a_ready);
+      // ---- (b) v^T = U^T - S^T W^T
+      float u[C];
+      {
+        const float4* up = reinterpret_cast<const float4*>(Ut + (ck * 128 + r) * C);
+#pragma unroll
+        for (int j = 0; j < C / 4; ++j) {
+          const float4 t = up[j];
+          u[4 * j] = t.x, u[4 * j + 1] = t.y, u[4 * j + 2] = t.z, u[4 * j + 3] = t.w;
+        }
+      }
+      ok = __all_sync(0xffffffff, sm100::mbar_wait(mm12, ch & 1, err));
+      if (!ok) break;
+      sm100::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < C; c += 32) {
+        float v[32];
+        sm100::tmem_ld32(tmem + lane_off + VN_COL + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = u[c + j] - v[j];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int ch16 = (c >> 3) + j;
+          *reinterpret_cast<uint4*>(sV + r * 128 + ((ch16 ^ (r & 7)) << 4)) = pack_bf16x8(v + 8 * j);
+        }
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(v_ready);
+    }
+    // output of the last chunk
+    if (ok && nchunks > 0) {
+      ok = __all_sync(0xffffffff, sm100::mbar_wait(mm34, (nchunks - 1) & 1, err));
+      if (ok) {
+        sm100::tc_fence_after();
+        const int t0 = (nchunks - 1) * C;
+        const int cnt = min(C, s - t0);
+#pragma unroll 1
+        for (int c = 0; c < C; c += 32) {
+          float o[32];
+          sm100::tmem_ld32(tmem + lane_off + O_COL + c, o);
+          for (int i = 0; i < 32 && c + i < cnt; ++i)
+            out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, tcs::TMEM_COLS);
+  }
+}
+
 }  // namespace gdn
 
 template <int D>
@@ -421,30 +754,60 @@ static void gdn_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::T
   const int nchunks = (s + C - 1) / C;
   const int64_t nck = (int64_t)b * nv * nchunks;
   auto f32 = q.options().dtype(at::kFloat);
-  at::Tensor WT = at::empty({nck * D * C}, f32);
-  at::Tensor AqkT = at::empty({nck * C * C}, f32);
-  at::Tensor U = at::empty({nck * C * D}, f32);
   at::Tensor GL = at::empty({nck}, f32);
-  at::Tensor QgT = at::empty({nck * D * C}, q.options());
+  at::Tensor U = at::empty({nck * C * D}, f32);
+  at::Tensor Qg = at::empty({nck * D * C}, q.options());
   at::Tensor Kd = at::empty({nck * C * D}, q.options());
-  static std::atomic<unsigned long long> attr{0};
-  once_per_device(attr, [&] {
-    NS_CUDA(cudaFuncSetAttribute(gdn_prep_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Prep<D>::BYTES));
-    NS_CUDA(cudaFuncSetAttribute(gdn_state_kernel<D, DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 State<D, DVS>::BYTES));
-  });
   const auto* bq = reinterpret_cast<const bf16*>(q.data_ptr());
-  gdn_prep_kernel<D><<<dim3(nchunks, nv, b), NT, Prep<D>::BYTES, stream()>>>(
-      bq, reinterpret_cast<const bf16*>(k.data_ptr()), reinterpret_cast<const bf16*>(v.data_ptr()),
-      g.data_ptr<float>(), reinterpret_cast<const bf16*>(beta.data_ptr()), s, nk, nv, groups, nchunks,
-      WT.data_ptr<float>(), reinterpret_cast<bf16*>(QgT.data_ptr()), reinterpret_cast<bf16*>(Kd.data_ptr()),
-      AqkT.data_ptr<float>(), U.data_ptr<float>(), GL.data_ptr<float>(), DVS);
-  NS_CUDA(cudaGetLastError());
-  gdn_state_kernel<D, DVS><<<dim3(D / DVS, nv, b), NT, State<D, DVS>::BYTES, stream()>>>(
-      WT.data_ptr<float>(), reinterpret_cast<const bf16*>(QgT.data_ptr()), reinterpret_cast<const bf16*>(Kd.data_ptr()),
-      AqkT.data_ptr<float>(), U.data_ptr<float>(), GL.data_ptr<float>(), reinterpret_cast<bf16*>(out.data_ptr()),
-      s, nv, nchunks, device_error_flag());
-  NS_CUDA(cudaGetLastError());
+  const auto* bk = reinterpret_cast<const bf16*>(k.data_ptr());
+  const auto* bv = reinterpret_cast<const bf16*>(v.data_ptr());
+  const auto* bb = reinterpret_cast<const bf16*>(beta.data_ptr());
+  if constexpr (D == 128) {
+    // tensor-core state recurrence: bf16 K-major operand tiles
+    at::Tensor W = at::empty({nck * C * D}, q.options());
+    at::Tensor A = at::empty({nck * C * C}, q.options());
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [&] {
+      NS_CUDA(cudaFuncSetAttribute(gdn_prep_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Prep<D>::BYTES));
+      NS_CUDA(cudaFuncSetAttribute(gdn_state_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcs::SMEM));
+    });
+    gdn_prep_kernel<D, true><<<dim3(nchunks, nv, b), NT, Prep<D>::BYTES, stream()>>>(
+        bq, bk, bv, g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, W.data_ptr(),
+        reinterpret_cast<bf16*>(Qg.data_ptr()), reinterpret_cast<bf16*>(Kd.data_ptr()), A.data_ptr(),
+        U.data_ptr<float>(), GL.data_ptr<float>(), DVS);
+    NS_CUDA(cudaGetLastError());
+    const int64_t rows = nck * C;
+    CUtensorMap tw = make_tmap_bf16(W.data_ptr(), rows, D, D, C, 64);
+    CUtensorMap tq = make_tmap_bf16(Qg.data_ptr(), rows, D, D, C, 64);
+    CUtensorMap ta = make_tmap_bf16(A.data_ptr(), rows, C, C, C, 64);
+    CUtensorMap tk = make_tmap_bf16(Kd.data_ptr(), nck * D, C, C, 128, 64);
+    gdn_state_tc_kernel<<<dim3(nv, b), 192, tcs::SMEM, stream()>>>(tw, tq, ta, tk, U.data_ptr<float>(),
+                                                                    GL.data_ptr<float>(),
+                                                                    reinterpret_cast<bf16*>(out.data_ptr()), s, nv,
+                                                                    nchunks, device_error_flag());
+    NS_CUDA(cudaGetLastError());
+  } else {
+    at::Tensor WT = at::empty({nck * D * C}, f32);
+    at::Tensor AqkT = at::empty({nck * C * C}, f32);
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [&] {
+      NS_CUDA(cudaFuncSetAttribute(gdn_prep_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Prep<D>::BYTES));
+      NS_CUDA(cudaFuncSetAttribute(gdn_state_kernel<D, DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   State<D, DVS>::BYTES));
+    });
+    gdn_prep_kernel<D, false><<<dim3(nchunks, nv, b), NT, Prep<D>::BYTES, stream()>>>(
+        bq, bk, bv, g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, WT.data_ptr(),
+        reinterpret_cast<bf16*>(Qg.data_ptr()), reinterpret_cast<bf16*>(Kd.data_ptr()), AqkT.data_ptr(),
+        U.data_ptr<float>(), GL.data_ptr<float>(), DVS);
+    NS_CUDA(cudaGetLastError());
+    gdn_state_kernel<D, DVS><<<dim3(D / DVS, nv, b), NT, State<D, DVS>::BYTES, stream()>>>(
+        WT.data_ptr<float>(), reinterpret_cast<const bf16*>(Qg.data_ptr()),
+        reinterpret_cast<const bf16*>(Kd.data_ptr()), AqkT.data_ptr<float>(), U.data_ptr<float>(),
+        GL.data_ptr<float>(), reinterpret_cast<bf16*>(out.data_ptr()), s, nv, nchunks, device_error_flag());
+    NS_CUDA(cudaGetLastError());
+  }
 }
 
 void gdn_chunk_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, int64_t groups,

@@ -139,37 +139,39 @@ __global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __rest
   }
 }
 
-// gu [T, 2m] = [gate | up]; h = bf16(bf16(silu(gate)) * up) -> e4m3 + scales [T, m/128]
+// gu [T, 2m] = [gate | up]; h = bf16(bf16(silu(gate)) * up) -> e4m3 + scales [T, m/128].
+// A 128-channel block per half-warp, 8 channels (16-byte loads) per lane.
 __global__ void silu_mul_quant_kernel(const bf16* __restrict__ gu, int64_t T, int m, uint8_t* __restrict__ q,
                                       float* __restrict__ s) {
-  const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const int64_t hw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;  // half-warp = one block
+  const int l16 = threadIdx.x & 15;
   const int kbs = m / 128;
-  if (wid >= T * kbs) return;
-  const int64_t t = wid / kbs;
-  const int kb = (int)(wid % kbs);
-  const bf16* g = gu + t * 2 * m + kb * 128 + lane * 4;
-  const bf16* u = g + m;
-  const uint2 gr = *reinterpret_cast<const uint2*>(g), ur = *reinterpret_cast<const uint2*>(u);
-  const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gr);
-  const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&ur);
-  float h[4];
+  const bool in = hw < T * kbs;
+  const int64_t t = in ? hw / kbs : 0;
+  const int kb = in ? (int)(hw % kbs) : 0;
+  float h[8];
   float am = 0.f;
+  if (in) {
+    const bf16* g = gu + t * 2 * m + kb * 128 + l16 * 8;
+    float gv[8], uv[8];
+    unpack8(*reinterpret_cast<const uint4*>(g), gv);
+    unpack8(*reinterpret_cast<const uint4*>(g + m), uv);
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float2 gf = __bfloat1622float2(gh[i]), uf = __bfloat1622float2(uh[i]);
-    const float a = rb(rb(gf.x / (1.f + expf(-gf.x))) * uf.x);
-    const float b = rb(rb(gf.y / (1.f + expf(-gf.y))) * uf.y);
-    h[2 * i] = a;
-    h[2 * i + 1] = b;
-    am = fmaxf(am, fmaxf(fabsf(a), fabsf(b)));
+    for (int i = 0; i < 8; ++i) {
+      h[i] = rb(rb(gv[i] / (1.f + expf(-gv[i]))) * uv[i]);
+      am = fmaxf(am, fabsf(h[i]));
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffff, am, o));
+  for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffff, am, o, 16));
+  if (!in) return;
   const float sc = am / 448.f;
   const float den = fmaxf(sc, 1.17549435e-38f);
-  *reinterpret_cast<uint32_t*>(q + t * m + kb * 128 + lane * 4) = e4m3x4_div(h[0], h[1], h[2], h[3], den);
-  if (lane == 0) s[t * kbs + kb] = sc;
+  uint2 pk;
+  pk.x = e4m3x4_div(h[0], h[1], h[2], h[3], den);
+  pk.y = e4m3x4_div(h[4], h[5], h[6], h[7], den);
+  *reinterpret_cast<uint2*>(q + t * m + kb * 128 + l16 * 8) = pk;
+  if (l16 == 0) s[t * kbs + kb] = sc;
 }
 
 // rows of 128 (row = token * nv + head): y = bf16(rb(w * rb(x * inv)) * silu(z)) ->
@@ -215,38 +217,45 @@ __global__ void gated_norm_quant_kernel(const bf16* __restrict__ x, const bf16* 
 }
 
 // out[b, t, c] = silu(bf16(sum_j w[c, j] x[b, t - (K-1) + j, c])); x rows of ld elements
-// (the first C channels of each row are convolved), 8 channels per thread.
+// (the first C channels of each row are convolved). blockIdx.x = token row b * s + t,
+// 8 channels per thread; K <= 4 taps.
 __global__ void conv_silu_vec_kernel(const bf16* __restrict__ x, int64_t ld, const bf16* __restrict__ w,
-                                     bf16* __restrict__ y, int s, int C, int K, int64_t total8) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c8 = (int)(i % (C / 8));
-    const int64_t bt = i / (C / 8);
-    const int t = (int)(bt % s);
-    const int c = c8 * 8;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < K; ++j) {
-      const int tt = t - (K - 1) + j;
-      if (tt < 0) continue;
-      float xv[8];
-      unpack8(*reinterpret_cast<const uint4*>(x + (bt - t + tt) * ld + c), xv);
+                                     bf16* __restrict__ y, int s, int C, int K) {
+  const int c8 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c8 * 8 >= C) return;
+  const int64_t bt = blockIdx.x;
+  const int t = (int)(bt % s);
+  const int c = c8 * 8;
+  float wv[8][4];
+  {
+    // w [C, K] row-major: the 8 channels' taps are 8 * K contiguous values
+    const bf16* wp = w + (int64_t)c * K;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(w[(c + e) * K + j]) * xv[e];
-    }
-    float o[8];
+    for (int e = 0; e < 8; ++e)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float zz = rb(acc[e]);
-      o[e] = zz / (1.f + expf(-zz));
-    }
-    reinterpret_cast<uint4*>(y + bt * C)[c8] = pack8(o);
+      for (int j = 0; j < 4; ++j) wv[e][j] = j < K ? __bfloat162float(wp[e * K + j]) : 0.f;
   }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= K) break;
+    const int tt = t - (K - 1) + j;
+    if (tt < 0) continue;
+    float xv[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + (bt - t + tt) * ld + c), xv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += wv[e][j] * xv[e];
+  }
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float zz = rb(acc[e]);
+    o[e] = zz / (1.f + expf(-zz));
+  }
+  reinterpret_cast<uint4*>(y + bt * C)[c8] = pack8(o);
 }
 
 }  // namespace vf
-
-static int grid_for(int64_t threads) {
-  return (int)std::max<int64_t>(1, std::min<int64_t>((threads + 255) / 256, (int64_t)num_sms() * 32));
-}
 
 // x_out / n_out / q_out+s_out optional (undefined tensors); y optional.
 void add_norm(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps, c10::optional<at::Tensor> x_out,
@@ -271,9 +280,9 @@ void silu_mul_quant(at::Tensor gu, at::Tensor q, at::Tensor s) {
   const int64_t T = gu.size(0);
   const int m = (int)(gu.size(1) / 2);
   NS_CHECK(gu.is_contiguous() && m % 128 == 0, "silu_mul_quant: [T, 2m] with m a multiple of 128");
-  const int64_t warps = T * (m / 128);
-  if (warps == 0) return;
-  vf::silu_mul_quant_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream()>>>(
+  const int64_t halfwarps = T * (m / 128);
+  if (halfwarps == 0) return;
+  vf::silu_mul_quant_kernel<<<(unsigned)((halfwarps * 16 + 255) / 256), 256, 0, stream()>>>(
       reinterpret_cast<const bf16*>(gu.data_ptr()), T, m, q.data_ptr<uint8_t>(), s.data_ptr<float>());
   NS_CUDA(cudaGetLastError());
 }
@@ -295,11 +304,13 @@ void gated_norm_quant(at::Tensor x, at::Tensor z, int64_t nv, int64_t z_ts, at::
 void conv_silu_vec(at::Tensor x, int64_t ld, at::Tensor w, at::Tensor y) {
   const int b = (int)y.size(0), s = (int)y.size(1), C = (int)y.size(2), K = (int)w.size(1);
   NS_CHECK(C % 8 == 0 && ld % 8 == 0 && y.is_contiguous(), "conv_silu_vec: 8-channel alignment");
-  const int64_t total8 = (int64_t)b * s * (C / 8);
-  if (total8 == 0) return;
-  vf::conv_silu_vec_kernel<<<grid_for(total8), 256, 0, stream()>>>(
-      reinterpret_cast<const bf16*>(x.data_ptr()), ld, reinterpret_cast<const bf16*>(w.data_ptr()),
-      reinterpret_cast<bf16*>(y.data_ptr()), s, C, K, total8);
+  NS_CHECK(K <= 4, "conv_silu_vec: kernel width <= 4");
+  const int64_t rows = (int64_t)b * s;
+  if (rows == 0) return;
+  const dim3 grid((unsigned)rows, (unsigned)((C / 8 + 255) / 256));
+  vf::conv_silu_vec_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), ld,
+                                                     reinterpret_cast<const bf16*>(w.data_ptr()),
+                                                     reinterpret_cast<bf16*>(y.data_ptr()), s, C, K);
   NS_CUDA(cudaGetLastError());
 }
 

@@ -217,7 +217,8 @@ def bench_verifier(a):
             setattr(vops, n, orig[n])
     per = {n: round(sum(e0.elapsed_time(e1) for e0, e1 in v) / a.reps, 3) for n, v in times.items()}
     gemm_ms = per.get("fp8_gemm", 0.0) + per.get("fp8_linear", 0.0)
-    return {"op": "verifier_4_layers", "S": a.S, "stage_ms": round(whole, 3), "op_ms": per,
+    kern = _kernel_times(lambda: stage_forward(st, ids), reps=2)
+    return {"op": "verifier_4_layers", "S": a.S, "stage_ms": round(whole, 3), "op_ms": per, "kernel_us": kern,
             "fp8_tflops": round(_verifier_fp8_flops(tc, a.S) / (gemm_ms * 1e9), 1) if gemm_ms else None}
 
 
