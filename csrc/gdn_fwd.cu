@@ -46,43 +46,63 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 template <int D>
 struct Prep {
-  static constexpr int DP = D + 4;                                   // padded row of [C][D] tiles
-  static constexpr int KT = D * CP;                                  // k^T
-  static constexpr int QX = (D * CP > C * DP) ? D * CP : C * DP;     // q^T, later beta k e^G
-  static constexpr int XV = C * DP;                                  // v, then beta v
-  static constexpr int MS = C * (C + 1);
+  static constexpr int DB = D + 4;                 // padded bf16 row of the [C][D] q / k / v tiles
+  static constexpr int TILE = C * DB * 2;          // bytes of one tile
+  static constexpr int MS = C * (C + 1);           // fp32 [C][C + 1]
   static constexpr int PS = 3 * 16 * 17;
-  static constexpr int FLOATS = KT + QX + XV + 2 * MS + PS + 4 * C;
-  static constexpr int BYTES = FLOATS * 4;
+  static constexpr int TR = D * CP * 4;            // fp32 transpose buffer [D][CP] (reuses q / k tiles)
+  static constexpr int QK = 2 * TILE > TR ? 2 * TILE : TR;
+  static constexpr int BYTES = QK + TILE + (2 * MS + PS + 5 * C) * 4;
 };
+
+__device__ __forceinline__ void ld_bf16x4(const bf16* p, float (&f)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+}
+
+__device__ __forceinline__ void st_bf16x4(bf16* p, float a, float b, float c, float d) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&lo);
+  u.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = u;
+}
 
 // Outputs per (row, head, chunk) ck, two layouts:
 //  TC = false (CUDA-core state kernel): WT fp32 [D][C], QgT bf16 [D][C], Kd bf16 [C][D],
 //      AqkT fp32 [C][C] (A transposed), U fp32 slice-major [D/dvs][C][dvs];
 //  TC = true (tensor-core state kernel, operands K-major for tcgen05): W bf16 [C][D],
 //      Qg bf16 [C][D], Kd^T bf16 [D][C], A bf16 [C][C], U^T fp32 [D][C].
-// GL fp32 = e^{G_last} either way.
+// GL fp32 = e^{G_last} either way. q / k / v rows are strided: token t of row b at
+// (b * s + t) * x_ts (elements), head offset h * D.
+// Shared memory holds the chunk's normalised q and k and raw v as bf16 rows (they are
+// bf16 values in the reference statement too), about 90 KB, so two CTAs share an SM.
 template <int D, bool TC>
-__global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                      const bf16* __restrict__ v, const float* __restrict__ gin,
-                                                      const bf16* __restrict__ beta_in, int s, int nk, int nv,
-                                                      int groups, int nchunks, void* __restrict__ Wo,
-                                                      bf16* __restrict__ QgO, bf16* __restrict__ KdO,
-                                                      void* __restrict__ AqkO, float* __restrict__ Uo,
-                                                      float* __restrict__ GL, int dvs) {
+__global__ void __launch_bounds__(NT, 2) gdn_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                         const bf16* __restrict__ v, int64_t q_ts, int64_t k_ts,
+                                                         int64_t v_ts, const float* __restrict__ gin,
+                                                         const bf16* __restrict__ beta_in, int s, int nk, int nv,
+                                                         int groups, int nchunks, void* __restrict__ Wo,
+                                                         bf16* __restrict__ QgO, bf16* __restrict__ KdO,
+                                                         void* __restrict__ AqkO, float* __restrict__ Uo,
+                                                         float* __restrict__ GL, int dvs) {
   using L = Prep<D>;
-  constexpr int DP = L::DP;
-  extern __shared__ __align__(16) float sm[];
-  float* kT = sm;
-  float* qT = kT + L::KT;  // later Xk
-  float* Xv = qT + L::QX;
-  float* Ms = Xv + L::XV;
+  constexpr int DB = L::DB;
+  extern __shared__ __align__(16) uint8_t smp[];
+  bf16* qs = reinterpret_cast<bf16*>(smp);             // [C][DB]
+  bf16* ks = qs + C * DB;                              // [C][DB]
+  bf16* vs = reinterpret_cast<bf16*>(smp + L::QK);     // [C][DB]
+  float* Ms = reinterpret_cast<float*>(smp + L::QK + L::TILE);
   float* Ts = Ms + L::MS;
   float* Ps = Ts + L::MS;
   float* G = Ps + L::PS;
   float* Bt = G + C;
   float* eG = Bt + C;
   float* eGl = eG + C;
+  float* fk = eGl + C;  // beta e^G
+  float* tr = reinterpret_cast<float*>(smp);           // [D][CP] transpose buffer (after q / k are consumed)
   const int ch = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
   const int hk = h / groups;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -90,31 +110,51 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
   const float scale = rsqrtf((float)D);
   const int64_t ck = ((int64_t)bi * nv + h) * nchunks + ch;
 
-  // 1. load; q and k L2-normalised as the bf16 statement computes them
-  for (int r = warp; r < C; r += NT / 32) {
-    const bool in = r < cnt;
-    const int64_t tq = (int64_t)bi * s + t0 + r;
-    float sq = 0.f, sk = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float a = in ? bf(q[(tq * nk + hk) * D + d]) : 0.f;
-      const float b = in ? bf(k[(tq * nk + hk) * D + d]) : 0.f;
-      sq += rb(a * a);
-      sk += rb(b * b);
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float iq = rb(rsqrtf(rb(rb(sq) + 1e-6f)));
-    const float ik = rb(rsqrtf(rb(rb(sk) + 1e-6f)));
-    for (int d = lane; d < D; d += 32) {
-      const float a = in ? bf(q[(tq * nk + hk) * D + d]) : 0.f;
-      const float b = in ? bf(k[(tq * nk + hk) * D + d]) : 0.f;
-      qT[d * CP + r] = rb(a * iq);
-      kT[d * CP + r] = rb(b * ik);
-      Xv[r * DP + d] = in ? bf(v[(tq * nv + h) * D + d]) : 0.f;
-    }
-    if (lane == 0) {
-      G[r] = in ? gin[tq * nv + h] : 0.f;
-      Bt[r] = in ? bf(beta_in[tq * nv + h]) : 0.f;
+  // 1. load; q and k L2-normalised as the bf16 statement computes them. Lane l holds
+  //    channels [4l, 4l + 4); two rows per step so their loads overlap.
+  {
+    constexpr int LANES = D / 4;  // active lanes per row
+    for (int r0 = warp * 2; r0 < C; r0 += 2 * (NT / 32)) {
+      float qa[2][4], ka[2][4], va[2][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = r0 + u;
+        const bool in = r < cnt && lane < LANES;
+        const int64_t tq = (int64_t)bi * s + t0 + r;
+        if (in) {
+          ld_bf16x4(q + tq * q_ts + hk * D + 4 * lane, qa[u]);
+          ld_bf16x4(k + tq * k_ts + hk * D + 4 * lane, ka[u]);
+          ld_bf16x4(v + tq * v_ts + h * D + 4 * lane, va[u]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) qa[u][e] = ka[u][e] = va[u][e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = r0 + u;
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          sq += rb(qa[u][e] * qa[u][e]);
+          sk += rb(ka[u][e] * ka[u][e]);
+        }
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        const float iq = rb(rsqrtf(rb(rb(sq) + 1e-6f)));
+        const float ik = rb(rsqrtf(rb(rb(sk) + 1e-6f)));
+        if (lane < LANES) {
+          st_bf16x4(qs + r * DB + 4 * lane, qa[u][0] * iq, qa[u][1] * iq, qa[u][2] * iq, qa[u][3] * iq);
+          st_bf16x4(ks + r * DB + 4 * lane, ka[u][0] * ik, ka[u][1] * ik, ka[u][2] * ik, ka[u][3] * ik);
+          st_bf16x4(vs + r * DB + 4 * lane, va[u][0], va[u][1], va[u][2], va[u][3]);
+        }
+        if (lane == 0) {
+          const bool in = r < cnt;
+          const int64_t tq = (int64_t)bi * s + t0 + r;
+          G[r] = in ? gin[tq * nv + h] : 0.f;
+          Bt[r] = in ? bf(beta_in[tq * nv + h]) : 0.f;
+        }
+      }
     }
   }
   __syncthreads();
@@ -136,14 +176,13 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
   if (tid < C) {
     eG[tid] = expf(G[tid]);
     eGl[tid] = expf(Gl - G[tid]);
+    fk[tid] = Bt[tid] * eG[tid];
   }
   __syncthreads();
 
-  // 2. M = strict_lower(beta_i k_i.k_j e^{G_i-G_j}) and A = lower(scale q_i.k_j e^{G_i-G_j});
-  //    each thread a 4 x 4 block of both. A goes to global memory transposed.
-  // Only the 136 blocks on or below the diagonal exist: thread t < 136 takes block
-  // (bi, bj) of the triangle, so no lane of a working warp idles through the loop;
-  // the blocks above the diagonal are zero and written by the remaining threads.
+  // 2. M = strict_lower(beta_i k_i.k_j e^{G_i-G_j}) and A = lower(scale q_i.k_j e^{G_i-G_j}).
+  //    Thread t < 136 takes block (bi, bj) of the lower triangle of 4 x 4 blocks and
+  //    walks d four channels at a time; the blocks above the diagonal are zero.
   {
     constexpr int NB = C / 4, TRI = NB * (NB + 1) / 2;
     float* at = reinterpret_cast<float*>(AqkO) + ck * C * C;   // TC = false: A^T fp32
@@ -159,20 +198,24 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c) kk[r][c] = qk[r][c] = 0.f;
-#pragma unroll 4
-      for (int d = 0; d < D; ++d) {
-        const float4 ki = *reinterpret_cast<const float4*>(&kT[d * CP + i0]);
-        const float4 qi = *reinterpret_cast<const float4*>(&qT[d * CP + i0]);
-        const float4 kj = *reinterpret_cast<const float4*>(&kT[d * CP + j0]);
-        const float kiv[4] = {ki.x, ki.y, ki.z, ki.w}, qiv[4] = {qi.x, qi.y, qi.z, qi.w};
-        const float kjv[4] = {kj.x, kj.y, kj.z, kj.w};
+#pragma unroll 2
+      for (int d = 0; d < D; d += 4) {
+        float ki[4][4], qi[4][4], kj[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          ld_bf16x4(ks + (i0 + r) * DB + d, ki[r]);
+          ld_bf16x4(qs + (i0 + r) * DB + d, qi[r]);
+          ld_bf16x4(ks + (j0 + r) * DB + d, kj[r]);
+        }
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            kk[r][c] = fmaf(kiv[r], kjv[c], kk[r][c]);
-            qk[r][c] = fmaf(qiv[r], kjv[c], qk[r][c]);
-          }
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              kk[r][c] = fmaf(ki[r][e], kj[c][e], kk[r][c]);
+              qk[r][c] = fmaf(qi[r][e], kj[c][e], qk[r][c]);
+            }
       }
       float a16[4][4];
 #pragma unroll
@@ -188,14 +231,7 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
       }
       if constexpr (TC) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          __nv_bfloat162 lo = __floats2bfloat162_rn(a16[r][0], a16[r][1]);
-          __nv_bfloat162 hi = __floats2bfloat162_rn(a16[r][2], a16[r][3]);
-          uint2 pk;
-          pk.x = *reinterpret_cast<uint32_t*>(&lo);
-          pk.y = *reinterpret_cast<uint32_t*>(&hi);
-          *reinterpret_cast<uint2*>(&ab[(i0 + r) * C + j0]) = pk;
-        }
+        for (int r = 0; r < 4; ++r) st_bf16x4(&ab[(i0 + r) * C + j0], a16[r][0], a16[r][1], a16[r][2], a16[r][3]);
       } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -203,7 +239,6 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
               make_float4(a16[0][c], a16[1][c], a16[2][c], a16[3][c]);
       }
     } else {
-      // zero blocks above the diagonal: (row block i, column block j), j > i
       for (int idx = tid - TRI; idx < NB * NB - TRI; idx += NT - TRI) {
         int i = 0, rem = idx;
         while (rem >= NB - 1 - i) {
@@ -223,39 +258,32 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
       }
     }
   }
-  __syncthreads();
-  // q scale e^G and k e^{G_last - G} for the state kernel (bf16)
+  // q scale e^G and k e^{G_last - G} for the state kernel (bf16), from the smem rows
   {
     bf16* qg = QgO + ck * D * C;
     bf16* kd = KdO + ck * C * D;
     if constexpr (TC) {
       for (int idx = tid; idx < C * D; idx += NT) {  // Qg [C][D]
         const int i = idx / D, d = idx % D;
-        qg[idx] = __float2bfloat16(qT[d * CP + i] * scale * eG[i]);
+        qg[idx] = __float2bfloat16(bf(qs[i * DB + d]) * scale * eG[i]);
       }
       for (int idx = tid; idx < D * C; idx += NT) {  // Kd^T [D][C]
         const int d = idx / C, i = idx % C;
-        kd[idx] = __float2bfloat16(kT[d * CP + i] * eGl[i]);
+        kd[idx] = __float2bfloat16(bf(ks[i * DB + d]) * eGl[i]);
       }
     } else {
       for (int idx = tid; idx < D * C; idx += NT) {  // Qg^T [D][C]
         const int d = idx / C, i = idx % C;
-        qg[idx] = __float2bfloat16(qT[d * CP + i] * scale * eG[i]);
+        qg[idx] = __float2bfloat16(bf(qs[i * DB + d]) * scale * eG[i]);
       }
       for (int idx = tid; idx < C * D; idx += NT) {  // Kd [C][D]
         const int i = idx / D, d = idx % D;
-        kd[idx] = __float2bfloat16(kT[d * CP + i] * eGl[i]);
+        kd[idx] = __float2bfloat16(bf(ks[i * DB + d]) * eGl[i]);
       }
     }
     if (tid == 0) GL[ck] = expf(Gl);
   }
   __syncthreads();
-  float* Xk = qT;
-  for (int idx = tid; idx < C * D; idx += NT) {
-    const int i = idx / D, d = idx % D;
-    Xk[i * DP + d] = Bt[i] * kT[d * CP + i] * eG[i];
-    Xv[i * DP + d] *= Bt[i];
-  }
 
   // 3. T = (I + M)^-1, blocked by 16. (a) diagonal blocks: thread c owns column c and
   //    keeps it in registers: T[i][c] = -sum_{m<i} M[i][m] T[m][c] below the diagonal.
@@ -298,7 +326,7 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
     __syncthreads();
   }
 
-  // 4. W = T (beta k e^G), U = T (beta v); W stored transposed, U slice-major
+  // 4. W = T (beta e^G k), U = T (beta v): the row factors are applied on the fly
   {
     constexpr int EG = D / 4, IG = NT / EG, RPT = C / IG;
     const int eg = tid % EG, i0 = (tid / EG) * RPT, e0 = eg * 4;
@@ -308,44 +336,40 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
 #pragma unroll
       for (int c = 0; c < 4; ++c) w[r][c] = u[r][c] = 0.f;
     for (int j = 0; j < i0 + RPT; ++j) {
-      const float4 xk = *reinterpret_cast<const float4*>(&Xk[j * DP + e0]);
-      const float4 xv = *reinterpret_cast<const float4*>(&Xv[j * DP + e0]);
+      float kv[4], vv[4];
+      ld_bf16x4(ks + j * DB + e0, kv);
+      ld_bf16x4(vs + j * DB + e0, vv);
+      const float fkj = fk[j], fvj = Bt[j];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kv[c] *= fkj;
+        vv[c] *= fvj;
+      }
 #pragma unroll
       for (int r = 0; r < RPT; ++r) {
         const float t = Ts[(i0 + r) * (C + 1) + j];
-        w[r][0] = fmaf(t, xk.x, w[r][0]);
-        w[r][1] = fmaf(t, xk.y, w[r][1]);
-        w[r][2] = fmaf(t, xk.z, w[r][2]);
-        w[r][3] = fmaf(t, xk.w, w[r][3]);
-        u[r][0] = fmaf(t, xv.x, u[r][0]);
-        u[r][1] = fmaf(t, xv.y, u[r][1]);
-        u[r][2] = fmaf(t, xv.z, u[r][2]);
-        u[r][3] = fmaf(t, xv.w, u[r][3]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          w[r][c] = fmaf(t, kv[c], w[r][c]);
+          u[r][c] = fmaf(t, vv[c], u[r][c]);
+        }
       }
     }
+    __syncthreads();  // q / k tiles consumed: their space becomes the transpose buffer
     if constexpr (TC) {
       // W bf16 [C][D] straight from registers; U^T fp32 [D][C] through shared memory
       bf16* wo = reinterpret_cast<bf16*>(Wo) + ck * C * D;
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(w[r][0], w[r][1]);
-        __nv_bfloat162 hi = __floats2bfloat162_rn(w[r][2], w[r][3]);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(&wo[(i0 + r) * D + e0]) = pk;
-      }
-      __syncthreads();
-      float* uts = qT;  // [D][CP]
+      for (int r = 0; r < RPT; ++r) st_bf16x4(&wo[(i0 + r) * D + e0], w[r][0], w[r][1], w[r][2], w[r][3]);
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int r = 0; r < RPT; ++r) uts[(e0 + c) * CP + i0 + r] = u[r][c];
+        for (int r = 0; r < RPT; ++r) tr[(e0 + c) * CP + i0 + r] = u[r][c];
       __syncthreads();
       float* ut = Uo + ck * D * C;
       for (int idx = tid; idx < D * C / 4; idx += NT) {
         const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
-        *reinterpret_cast<float4*>(&ut[e * C + i4]) = *reinterpret_cast<const float4*>(&uts[e * CP + i4]);
+        *reinterpret_cast<float4*>(&ut[e * C + i4]) = *reinterpret_cast<const float4*>(&tr[e * CP + i4]);
       }
     } else {
       const int slice = e0 / dvs, el = e0 % dvs;
@@ -353,19 +377,15 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(const bf16* __restrict__ q
 #pragma unroll
       for (int r = 0; r < RPT; ++r)
         *reinterpret_cast<float4*>(&uo[(i0 + r) * dvs + el]) = make_float4(u[r][0], u[r][1], u[r][2], u[r][3]);
-      // W^T: transpose through shared memory (the q^T / beta k e^G area is free now),
-      // then write [D][C] rows with coalesced 16-byte stores
-      __syncthreads();
-      float* wts = qT;  // [D][CP]
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int r = 0; r < RPT; ++r) wts[(e0 + c) * CP + i0 + r] = w[r][c];
+        for (int r = 0; r < RPT; ++r) tr[(e0 + c) * CP + i0 + r] = w[r][c];
       __syncthreads();
       float* wt = reinterpret_cast<float*>(Wo) + ck * D * C;
       for (int idx = tid; idx < D * C / 4; idx += NT) {
         const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
-        *reinterpret_cast<float4*>(&wt[e * C + i4]) = *reinterpret_cast<const float4*>(&wts[e * CP + i4]);
+        *reinterpret_cast<float4*>(&wt[e * C + i4]) = *reinterpret_cast<const float4*>(&tr[e * CP + i4]);
       }
     }
   }
@@ -773,7 +793,7 @@ static void gdn_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::T
       NS_CUDA(cudaFuncSetAttribute(gdn_state_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcs::SMEM));
     });
     gdn_prep_kernel<D, true><<<dim3(nchunks, nv, b), NT, Prep<D>::BYTES, stream()>>>(
-        bq, bk, bv, g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, W.data_ptr(),
+        bq, bk, bv, q.stride(1), k.stride(1), v.stride(1), g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, W.data_ptr(),
         reinterpret_cast<bf16*>(Qg.data_ptr()), reinterpret_cast<bf16*>(Kd.data_ptr()), A.data_ptr(),
         U.data_ptr<float>(), GL.data_ptr<float>(), DVS);
     NS_CUDA(cudaGetLastError());
@@ -798,7 +818,7 @@ static void gdn_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::T
                                    State<D, DVS>::BYTES));
     });
     gdn_prep_kernel<D, false><<<dim3(nchunks, nv, b), NT, Prep<D>::BYTES, stream()>>>(
-        bq, bk, bv, g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, WT.data_ptr(),
+        bq, bk, bv, q.stride(1), k.stride(1), v.stride(1), g.data_ptr<float>(), bb, s, nk, nv, groups, nchunks, WT.data_ptr(),
         reinterpret_cast<bf16*>(Qg.data_ptr()), reinterpret_cast<bf16*>(Kd.data_ptr()), AqkT.data_ptr(),
         U.data_ptr<float>(), GL.data_ptr<float>(), DVS);
     NS_CUDA(cudaGetLastError());
@@ -814,9 +834,15 @@ void gdn_chunk_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::T
                    at::Tensor out) {
   NS_CHECK(q.size(3) == v.size(3), "gated delta rule kernel needs d_k == d_v");
   NS_CHECK(g.scalar_type() == at::kFloat, "g must be fp32");
-  NS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && g.is_contiguous() && beta.is_contiguous() &&
-               out.is_contiguous(),
-           "gated delta rule inputs must be contiguous");
+  NS_CHECK(g.is_contiguous() && beta.is_contiguous() && out.is_contiguous(), "g, beta and out must be contiguous");
+  // q / k / v: [b, s, heads, D] views with contiguous heads and one token stride (rows of
+  // a fused projection are fine); 8-byte aligned rows for the 4-channel loads
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    NS_CHECK(t->stride(3) == 1 && t->stride(2) == t->size(3) && t->stride(0) == t->size(1) * t->stride(1),
+             "gated delta rule: q / k / v must be [b, s, heads, D] rows with one token stride");
+    NS_CHECK(t->stride(1) % 4 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 8 == 0,
+             "gated delta rule: 8-byte aligned rows");
+  }
   if (q.size(1) == 0) return;
   switch (q.size(3)) {
     case 16: gdn_fwd_launch<16>(q, k, v, g, beta, (int)groups, out); break;

@@ -134,8 +134,10 @@ __global__ void __launch_bounds__(192, 1) vattn_fwd_kernel(const __grid_constant
   uint64_t* s_free = bars + 7;     // [2]
   uint64_t* p_full = bars + 9;     // [2]
   uint64_t* p_free = bars + 11;    // [2]
-  uint64_t* o_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* o_done = bars + 13;    // one completion per PV_j (rescales wait for PV_{j-1})
+  uint64_t* o_last = bars + 14;    // completes once, after the last PV (the epilogue's wait:
+                                   // a parity wait on o_done could be two phases behind there)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = gridDim.x - 1 - blockIdx.x;  // heavy tiles first
@@ -156,6 +158,7 @@ __global__ void __launch_bounds__(192, 1) vattn_fwd_kernel(const __grid_constant
       sm100::mbar_init(&p_free[i], 1);
     }
     sm100::mbar_init(o_done, 1);
+    sm100::mbar_init(o_last, 1);
     sm100::fence_barrier_init();
     sm100::tma_prefetch_desc(&tq);
     sm100::tma_prefetch_desc(&tk);
@@ -232,6 +235,7 @@ __global__ void __launch_bounds__(192, 1) vattn_fwd_kernel(const __grid_constant
           sm100::mma_bf16(tmem, ad, bd, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
         }
         sm100::mma_commit(o_done);
+        if (t == nkt - 1) sm100::mma_commit(o_last);
         sm100::mma_commit(&p_free[pb]);
         sm100::mma_commit(&kv_empty[t & 1]);
       }
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(192, 1) vattn_fwd_kernel(const __grid_constant
       if (lane == 0) sm100::mbar_arrive(&p_full[sb]);
     }
     // epilogue: out = bf16(O / l) * bf16(sigmoid(gate))
-    if (ok) ok = __all_sync(0xffffffff, sm100::mbar_wait(o_done, (nkt - 1) & 1, a.err));
+    if (ok) ok = __all_sync(0xffffffff, sm100::mbar_wait(o_last, 0, a.err));
     if (ok) {
       sm100::tc_fence_after();
       const float inv = 1.f / l;

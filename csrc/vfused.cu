@@ -217,42 +217,77 @@ __global__ void gated_norm_quant_kernel(const bf16* __restrict__ x, const bf16* 
 }
 
 // out[b, t, c] = silu(bf16(sum_j w[c, j] x[b, t - (K-1) + j, c])); x rows of ld elements
-// (the first C channels of each row are convolved). blockIdx.x = token row b * s + t,
-// 8 channels per thread; K <= 4 taps.
-__global__ void conv_silu_vec_kernel(const bf16* __restrict__ x, int64_t ld, const bf16* __restrict__ w,
-                                     bf16* __restrict__ y, int s, int C, int K) {
+// (the first C channels of each row are convolved). A thread owns 8 channels and a run
+// of CONV_TOKENS consecutive token rows: its 8 x K weights are loaded once (16-byte
+// loads), and the K - 1 previous rows are kept in registers, so every input row is read
+// once. Rows of a new sequence (t % s == 0) start with an empty window. K <= 4.
+constexpr int CONV_TOKENS = 16;
+
+__global__ void __launch_bounds__(256) conv_silu_vec_kernel(const bf16* __restrict__ x, int64_t ld,
+                                                            const bf16* __restrict__ w, bf16* __restrict__ y,
+                                                            int64_t rows, int s, int C, int K) {
   const int c8 = blockIdx.y * blockDim.x + threadIdx.x;
   if (c8 * 8 >= C) return;
-  const int64_t bt = blockIdx.x;
-  const int t = (int)(bt % s);
   const int c = c8 * 8;
   float wv[8][4];
   {
-    // w [C, K] row-major: the 8 channels' taps are 8 * K contiguous values
+    // w [C, K] row-major: this thread's 8 channels are 8 * K contiguous values
+    __align__(16) bf16 wr[32];
     const bf16* wp = w + (int64_t)c * K;
+    if (K == 4) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(wr)[i] = reinterpret_cast<const uint4*>(wp)[i];
+    } else {
+      for (int i = 0; i < 8 * K; ++i) wr[i] = wp[i];
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wv[e][j] = j < K ? __bfloat162float(wp[e * K + j]) : 0.f;
+      for (int j = 0; j < 4; ++j) wv[e][j] = j < K ? __bfloat162float(wr[e * K + j]) : 0.f;
   }
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const int64_t r0 = (int64_t)blockIdx.x * CONV_TOKENS;
+  const int64_t r1 = min(rows, r0 + CONV_TOKENS);
+  // window[j] = x row (t - 3 + j) for j = 0..2, zero before the sequence start
+  float win[3][8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (j >= K) break;
-    const int tt = t - (K - 1) + j;
-    if (tt < 0) continue;
-    float xv[8];
-    unpack8(*reinterpret_cast<const uint4*>(x + (bt - t + tt) * ld + c), xv);
+  for (int j = 0; j < 3; ++j) {
+    const int64_t rr = r0 - 3 + j;
+    const int back = 3 - j;  // rows before r0
+    const bool ok = rr >= 0 && (int)(r0 % s) >= back;
+    if (ok) unpack8(*reinterpret_cast<const uint4*>(x + rr * ld + c), win[j]);
+    else
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] += wv[e][j] * xv[e];
+      for (int e = 0; e < 8; ++e) win[j][e] = 0.f;
   }
-  float o[8];
+  for (int64_t r = r0; r < r1; ++r) {
+    if (r % s == 0 && r != r0) {
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float zz = rb(acc[e]);
-    o[e] = zz / (1.f + expf(-zz));
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) win[j][e] = 0.f;
+    }
+    float cur[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + r * ld + c), cur);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      // taps j = 0..K-1 read rows t - (K-1) + j: the last K entries of [win0, win1, win2, cur]
+      float acc = 0.f;
+      const float seq[4] = {win[0][e], win[1][e], win[2][e], cur[e]};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < K) acc += wv[e][j] * seq[4 - K + j];
+      const float zz = rb(acc);
+      o[e] = zz / (1.f + expf(-zz));
+    }
+    reinterpret_cast<uint4*>(y + r * C)[c8] = pack8(o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      win[0][e] = win[1][e];
+      win[1][e] = win[2][e];
+      win[2][e] = cur[e];
+    }
   }
-  reinterpret_cast<uint4*>(y + bt * C)[c8] = pack8(o);
 }
 
 }  // namespace vf
@@ -304,13 +339,15 @@ void gated_norm_quant(at::Tensor x, at::Tensor z, int64_t nv, int64_t z_ts, at::
 void conv_silu_vec(at::Tensor x, int64_t ld, at::Tensor w, at::Tensor y) {
   const int b = (int)y.size(0), s = (int)y.size(1), C = (int)y.size(2), K = (int)w.size(1);
   NS_CHECK(C % 8 == 0 && ld % 8 == 0 && y.is_contiguous(), "conv_silu_vec: 8-channel alignment");
-  NS_CHECK(K <= 4, "conv_silu_vec: kernel width <= 4");
+  NS_CHECK(K >= 1 && K <= 4, "conv_silu_vec: kernel width 1..4");
+  NS_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+           "conv_silu_vec: 16-byte aligned operands");
   const int64_t rows = (int64_t)b * s;
   if (rows == 0) return;
-  const dim3 grid((unsigned)rows, (unsigned)((C / 8 + 255) / 256));
+  const dim3 grid((unsigned)((rows + vf::CONV_TOKENS - 1) / vf::CONV_TOKENS), (unsigned)((C / 8 + 255) / 256));
   vf::conv_silu_vec_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), ld,
                                                      reinterpret_cast<const bf16*>(w.data_ptr()),
-                                                     reinterpret_cast<bf16*>(y.data_ptr()), s, C, K);
+                                                     reinterpret_cast<bf16*>(y.data_ptr()), rows, s, C, K);
   NS_CUDA(cudaGetLastError());
 }
 

@@ -105,13 +105,21 @@ def gated_delta_rule(q, k, v, g, beta, groups=1, chunk=64):
     """
     if q.is_cuda:
         out = torch.empty(v.shape, device=v.device, dtype=v.dtype)
-        _c().gdn_chunk_fwd(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(), beta.contiguous(),
-                           int(groups), out)
+        _c().gdn_chunk_fwd(_rows(q), _rows(k), _rows(v), g.contiguous(), beta.contiguous(), int(groups), out)
         return out
     if groups > 1:
         q = q.repeat_interleave(groups, 2)
         k = k.repeat_interleave(groups, 2)
     return ref.gated_delta_rule_chunked(q, k, v, g, beta, chunk)
+
+
+def _rows(t):
+    """``t`` [b, s, heads, D] as the kernels read it: contiguous heads and one token
+    stride (a view into a fused projection qualifies); otherwise a contiguous copy."""
+    b, s, h, d = t.shape
+    ok = (t.stride(3) == 1 and t.stride(2) == d and t.stride(0) == s * t.stride(1) and t.stride(1) % 4 == 0
+          and t.data_ptr() % 8 == 0)
+    return t if ok else t.contiguous()
 
 
 def rotary_factors(positions, dim, theta, dtype):

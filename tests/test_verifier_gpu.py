@@ -51,6 +51,11 @@ def test_small_verifier_ops():
           ref.qwen_gated_norm(x.view(-1, 96), gt, w, 1e-6), rtol=2e-2)
     cw = (torch.randn(96, 1, 4) * 0.3).bfloat16()
     close(vops.causal_conv_silu(x.cuda(), cw.cuda()), ref.causal_conv_silu(x, cw), rtol=2e-2)
+    # the row-strided, token-windowed conv of the fused path: the first 96 channels of
+    # 160-wide rows, three sequences of 50 tokens (windows straddle sequence starts)
+    xr = torch.randn(3, 50, 160).bfloat16()
+    close(vops.causal_conv_silu_rows(xr.cuda(), 160, cw.cuda(), 96), ref.causal_conv_silu(xr[..., :96], cw),
+          rtol=2e-2)
     a, b = torch.randn(3, 50, 6).bfloat16(), torch.randn(3, 50, 6).bfloat16()
     alog, dtb = torch.randn(6), torch.rand(6)
     g1, b1 = vops.gdn_gates(a.cuda(), b.cuda(), alog.cuda(), dtb.cuda())
