@@ -70,6 +70,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="one rank: run eagerly, not as a CUDA graph")
+    p.add_argument("--kernel-table", action="store_true",
+                   help="ours: print the device time of every kernel of one step to stderr")
     p.add_argument("--comm", choices=("peer", "nccl"), default="peer",
                    help="N>1: peer-memory kernels over NVLink (default) or NCCL collectives")
     return p.parse_args()
@@ -414,7 +416,31 @@ def profile_step(step_fn):
         return n, float("nan"), float("nan")
 
 
+def _kernel_table(step_fn, top=40):
+    """Device microseconds per kernel name over one step (torch.profiler), to stderr."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    agg = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            name = e.name.split("(")[0].replace("void ", "").strip()[:90]
+            t, n = agg.get(name, (0.0, 0))
+            agg[name] = (t + e.device_time_total, n + 1)
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][0])[:top]
+    total = sum(t for t, _ in agg.values())
+    print(f"kernel table: {total / 1000:.2f} ms device time in one step", file=sys.stderr)
+    for name, (t, n) in rows:
+        print(f"  {t / 1000:9.3f} ms  {n:5d}x  {name}", file=sys.stderr)
+
+
 def main():
+    # stdout carries exactly one JSON line (rank 0); anything a library prints on the
+    # process's stdout (NCCL's version banner, for one) is sent to stderr instead.
+    global _OUT_FD
+    _OUT_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     full = args.workload == "full"
     if args.seq_len is None:
@@ -496,6 +522,8 @@ def main():
         phase = None
         if args.impl == "ours" and full:
             phase = wl.phase_ms(dev)
+        if args.impl == "ours" and args.kernel_table and rank == 0:
+            _kernel_table(lambda: wl.step(*inputs))
         launches = comm_ms = exposed_ms = None
         if args.impl == "ours" and not args.no_count:
             per_step, comm, exposed = profile_step(lambda: wl.step(*inputs))
@@ -559,7 +587,7 @@ def main():
         if args.impl == "reference":
             out["impl"] = "reference"
         out["provenance"] = _provenance(world)
-        print(json.dumps(out), flush=True)
+        _emit(out)
     wl.close(world)
     if world > 1:
         dist.barrier()
@@ -580,10 +608,20 @@ def _provenance(world):
     return p
 
 
+_OUT_FD = None
+
+
+def _emit(obj):
+    """Write the result line to the original stdout."""
+    sys.stdout.flush()
+    line = (json.dumps(obj) + "\n").encode()
+    os.write(_OUT_FD if _OUT_FD is not None else 1, line)
+
+
 def _print_unavailable(n, why, args):
     rank = int(os.environ.get("RANK", 0))
     if rank == 0:
-        print(json.dumps({"impl": "reference", "unavailable": why, "n_gpus": n, "metric": METRIC}), flush=True)
+        _emit({"impl": "reference", "unavailable": why, "n_gpus": n, "metric": METRIC})
 
 
 if __name__ == "__main__":
