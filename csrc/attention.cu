@@ -22,6 +22,9 @@
 //                   head's CTA writes fp32 partials, summed in head order). A CTA
 //                   walks the query blocks that see its tile and accumulates dK, dV
 //                   in registers in a fixed order: deterministic, no atomics.
+#include <cstdlib>
+#include <string>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -721,9 +724,30 @@ static void bwd_d(AttnArgs a) {
   dkv_launch<D, RMAX, true, false>(a, a.nb);
 }
 
+bool dattn_supported(const at::Tensor& q, const at::Tensor& k, int64_t bs);
+void dattn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
+               at::Tensor out, at::Tensor lse);
+void dattn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
+               at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs, at::Tensor dq, at::Tensor dk,
+               at::Tensor dv);
+
+// Head dims 64 and 128 run on tensor cores (dattn.cu); the kernels of this file serve
+// the other head sizes. NANOSPEC_DRAFT_ATTN=cuda forces this file's kernels.
+static bool use_tc(const at::Tensor& q, const at::Tensor& k, int64_t bs) {
+  static const bool forced = [] {
+    const char* e = std::getenv("NANOSPEC_DRAFT_ATTN");
+    return e && std::string(e) == "cuda";
+  }();
+  return !forced && dattn_supported(q, k, bs);
+}
+
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor anchors, at::Tensor keep, int64_t S, int64_t bs,
               at::Tensor out, at::Tensor lse) {
   AttnArgs a = make_args(q, k, v, anchors, keep, S, bs);
+  if (use_tc(q, k, bs)) {
+    dattn_fwd(q, k, v, anchors, keep, S, bs, out, lse);
+    return;
+  }
   a.out = reinterpret_cast<bf16*>(out.data_ptr());
   a.lse = lse.data_ptr<float>();
   switch (q.size(3)) {
@@ -741,6 +765,10 @@ void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Ten
   AttnArgs a = make_args(q, k, v, anchors, keep, S, bs);
   NS_CHECK(dout.is_contiguous() && out.is_contiguous() && dq.is_contiguous(), "dout/out/dq must be contiguous");
   NS_CHECK(dk.stride(2) == 1 && dv.stride(2) == 1, "dk/dv must have dense heads");
+  if (use_tc(q, k, bs) && dk.stride(1) == dk.size(2) && dv.stride(1) == dv.size(2)) {
+    dattn_bwd(dout, q, k, v, out, lse, anchors, keep, S, bs, dq, dk, dv);
+    return;
+  }
   a.dout = reinterpret_cast<const bf16*>(dout.data_ptr());
   a.o = reinterpret_cast<const bf16*>(out.data_ptr());
   a.lse = lse.data_ptr<float>();

@@ -26,7 +26,9 @@ struct F8Cfg {
   static constexpr int STAGE = F8_BM * F8_BK + BN * F8_BK;  // bytes
   static constexpr int STAGES = BN == 256 ? 4 : 6;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 512;
-  static constexpr int PWARPS = BN / 32;                    // promotion warps: 128 columns each per quarter
+  static constexpr int CPW = 128;                           // columns promoted per warp
+  static constexpr int SEGS = BN / CPW;                     // column segments per TMEM lane quarter
+  static constexpr int PWARPS = 4 * SEGS;                   // promotion warps
   static constexpr int THREADS = 64 + 32 * PWARPS;
   static constexpr int TMEM_COLS = 2 * BN;                  // two partial buffers
 };
@@ -59,8 +61,10 @@ struct F8Args {
 // buffers and every barrier phase continue across tile boundaries (a global K-block
 // counter `it`), so the next tile's MMAs start while this tile's last partial is
 // promoted and stored. Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2.. the
-// promotion warps (BN / 32 of them; warp w owns TMEM lane quarter w % 4 and the
-// 128-column half (w - 2) / 4 of the tile, whose weight scale is one block).
+// promotion warps (4 * BN / 128 of them; warp w owns TMEM lane quarter w % 4 and the
+// 128-column segment (w - 2) / 4 of the tile, which is one 128-wide weight-scale
+// block). Sixteen warps of 64 columns each were measured slower: the register cap of
+// 576 threads spills the accumulators.
 template <int BN>
 __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, F8Args args) {
@@ -150,8 +154,9 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
       }
     }
   } else {
+    constexpr int CPW = C::CPW;
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int seg = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const int kbs = (args.K + 127) / 128;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
@@ -160,10 +165,10 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
     for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
       const int m0 = (tile % mt) * F8_BM, n0 = (tile / mt) * BN;
       const int m = m0 + row;
-      const int nb = n0 / 128 + half;
-      float acc[128];
+      const int nb = (n0 + seg * CPW) / 128;
+      float acc[CPW];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < CPW; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int buf = it & 1;
         ok = sm100::mbar_wait(&tfull[buf], (it >> 1) & 1, args.err);
@@ -173,9 +178,9 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
         const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + kb] : 0.f;
         const float f = sav * sbv;
 #pragma unroll
-        for (int c = 0; c < 128; c += 32) {
+        for (int c = 0; c < CPW; c += 32) {
           float v[32];
-          sm100::tmem_ld32(tmem + lane_off + (uint32_t)(buf * BN + half * 128 + c), v);
+          sm100::tmem_ld32(tmem + lane_off + (uint32_t)(buf * BN + seg * CPW + c), v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[c + j] = fmaf(f, v[j], acc[c + j]);
         }
@@ -183,10 +188,9 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
         sm100::mbar_arrive(&tempty[buf]);
       }
       if (ok && m < args.M) {
-        __nv_bfloat16* o = args.out + (int64_t)m * args.ldo + n0 + half * 128;
-        uint4* p = reinterpret_cast<uint4*>(o);
+        uint4* p = reinterpret_cast<uint4*>(args.out + (int64_t)m * args.ldo + n0 + seg * CPW);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < CPW / 8; ++j) {
           __nv_bfloat162 h[4];
 #pragma unroll
           for (int t = 0; t < 4; ++t) h[t] = __floats2bfloat162_rn(acc[8 * j + 2 * t], acc[8 * j + 2 * t + 1]);

@@ -314,11 +314,19 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dp, const bf16* __res
 }
 
 // ------------------------------------------------------------------ embedding
+// Token ids outside [0, rows) are not read: the row is written as zeros and the
+// device error word records code 3 (the host raises; see utils/health.py).
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ w, int d,
-                                     bf16* __restrict__ out, int64_t n) {
+                                     bf16* __restrict__ out, int64_t n, int64_t rows, int* err) {
   const int64_t t = blockIdx.x;
-  const bf16* src = w + ids[t] * (int64_t)d;
+  const int64_t id = ids[t];
   bf16* dst = out + t * d;
+  if (id < 0 || id >= rows) {
+    if (threadIdx.x == 0) atomicExch(err, 3);
+    for (int j = threadIdx.x; j < d; j += blockDim.x) dst[j] = __float2bfloat16(0.f);
+    return;
+  }
+  const bf16* src = w + id * (int64_t)d;
   if ((d % 8) == 0) {
     const uint4* s4 = reinterpret_cast<const uint4*>(src);
     uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -330,11 +338,16 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const bf16
 
 // grad[ids[i]] += dy[i] in token order; one thread per column: deterministic, no atomics.
 __global__ void embedding_bwd_kernel(const bf16* __restrict__ dy, const int64_t* __restrict__ ids,
-                                     int64_t tokens, int d, bf16* __restrict__ grad) {
+                                     int64_t tokens, int d, bf16* __restrict__ grad, int64_t rows, int* err) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
   for (int64_t i = 0; i < tokens; ++i) {
-    bf16* p = grad + ids[i] * (int64_t)d + c;
+    const int64_t id = ids[i];
+    if (id < 0 || id >= rows) {  // out of range: skipped, code 3 (see embedding_fwd_kernel)
+      if (c == 0) atomicExch(err, 3);
+      continue;
+    }
+    bf16* p = grad + id * (int64_t)d + c;
     *p = __float2bfloat16(f(*p) + f(dy[i * d + c]));
   }
 }
@@ -693,7 +706,8 @@ void embedding_fwd(at::Tensor ids, at::Tensor w, at::Tensor out) {
   const int64_t n = ids.numel();
   if (n == 0) return;
   embedding_fwd_kernel<<<n, 128, 0, stream()>>>(ids.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(w.data_ptr()),
-                                                w.size(1), reinterpret_cast<bf16*>(out.data_ptr()), n);
+                                                w.size(1), reinterpret_cast<bf16*>(out.data_ptr()), n, w.size(0),
+                                                device_error_flag());
   NS_CUDA(cudaGetLastError());
 }
 
@@ -703,7 +717,7 @@ void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor grad) {
   const int d = grad.size(1);
   embedding_bwd_kernel<<<(d + 127) / 128, 128, 0, stream()>>>(
       reinterpret_cast<const bf16*>(dy.data_ptr()), ids.data_ptr<int64_t>(), ids.numel(), d,
-      reinterpret_cast<bf16*>(grad.data_ptr()));
+      reinterpret_cast<bf16*>(grad.data_ptr()), grad.size(0), device_error_flag());
   NS_CUDA(cudaGetLastError());
 }
 

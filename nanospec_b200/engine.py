@@ -33,6 +33,7 @@ from .config import Objective
 from .data import prepare
 from .objective import LossMetrics, head_loss
 from .parallel.node import TeacherBatch
+from .utils import debug as _debug
 
 
 @dataclass
@@ -80,6 +81,8 @@ def _bind_grads(sched, index, unit):
             # One rank and a zero gradient shard: write gradients straight into it.
             buf = unit.grad
             unit.direct_grad = True
+            if _debug.enabled():  # copy semantics: every element must be overwritten
+                _debug.poison(buf[:unit.numel])
         else:
             buf = torch.empty(unit.full_size, device=unit.param.device, dtype=unit.param.dtype)
     if buf is not unit.grad:
@@ -353,6 +356,8 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
             phases.mark("verifier")
         if health is not None:
             health.snapshot("verifier")
+            if _debug.enabled():
+                health.check(block=True)
     if drafter is None:
         return TrainResult(teacher=teacher_batch)
     if teacher_batch is None or objective is None:
@@ -365,6 +370,8 @@ def train(ids, drafter=None, objective=None, *, verifier=None, teacher_batch=Non
                                resident, timer=phases)
     if health is not None:
         health.snapshot("draft forward/backward")
+        if _debug.enabled():
+            health.check(block=True)
     update = None
     if optimizer is not None:
         from .parallel.optim import adamw_step

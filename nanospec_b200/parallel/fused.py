@@ -39,6 +39,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops._ext import cuda_ops
+from ..utils import debug as _debug
 from .shard import ScheduleError
 
 FLAGS_BYTES = 4096
@@ -208,6 +209,8 @@ class PeerSchedule:
         # Every peer must have pulled this slot's previous contents.
         self._wait(CH_PULLED + slot, self.seq[CH_PULLED + slot])
         self.slot_owner[slot] = index
+        if _debug.enabled():  # every element must be rewritten by this unit's backward
+            _debug.poison(self.w.slots[slot][:unit.full_size])
         return self.w.slots[slot][:unit.full_size]
 
     def release(self, index):

@@ -29,6 +29,8 @@ from dataclasses import dataclass, field
 import torch
 import torch.distributed as dist
 
+from ..utils import debug as _debug
+
 
 class ScheduleError(RuntimeError):
     """Raised when a schedule's state machine is driven out of order."""
@@ -380,6 +382,8 @@ class OverlapSchedule:
         unit, slot = self._slot(index)
         if slot.owner != index or not slot.bound:
             raise ScheduleError("Release exactly one acquired unit")
+        if _debug.enabled():  # compute is done with the slot: stale reads become NaN
+            _debug.poison(slot.weights)
         slot.free.record(self.compute)
         slot.used_free = True
         unit.release()

@@ -20,7 +20,8 @@ the host has already synchronised when the optimizer reads its scalars). So a
 timeout raises in the same ``train()`` call with the default synchronous
 optimizer, or at the start of the next call otherwise.
 
-Codes: 1 = an mbarrier wait in a tensor-core kernel, 2 = a peer flag wait.
+Codes: 1 = an mbarrier wait in a tensor-core kernel, 2 = a peer flag wait, 3 = a
+token id outside the embedding table (the kernel skipped the access).
 Reference policy: the reference raises on schedule misuse
 (nanospec/shard.py:230-231,247-248) and relies on a finite NCCL timeout
 (nanospec/distributed.py:24); it has no device-side waits of its own.
@@ -32,16 +33,19 @@ import torch
 
 from ..ops._ext import cuda_ops
 
-CODES = {1: "a tensor-core kernel's mbarrier wait", 2: "a peer-memory flag wait"}
+CODES = {1: "a tensor-core kernel's mbarrier wait", 2: "a peer-memory flag wait",
+         3: "an index out of range in an embedding gather or scatter (the access was skipped)"}
 
 
 class DeviceWaitTimeout(RuntimeError):
-    """A bounded device-side wait gave up; the step's results are not valid."""
+    """A bounded device-side wait gave up (or a kernel skipped an out-of-range
+    access); the step's results are not valid."""
 
     def __init__(self, code: int, tag: str):
         self.code, self.tag = code, tag
         what = CODES.get(code, f"error code {code}")
-        super().__init__(f"{what} timed out on the device during '{tag}'; the step's outputs are invalid "
+        verb = "was reported" if code == 3 else "timed out"
+        super().__init__(f"{what} {verb} on the device during '{tag}'; the step's outputs are invalid "
                          f"(device state was reset)")
 
 

@@ -262,3 +262,24 @@ def test_device_wait_timeout_raises_on_host(monkeypatch, lag):
     flaky.phase, flaky.lag, flaky.landed = None, False, True  # the next step is clean again
     r = _step(c, m, opt)
     assert bool(r.update["updated"])
+
+
+def test_debug_mode_poison_leaves_results_unchanged(monkeypatch):
+    """NANOSPEC_DEBUG=1 fills every gradient shard the backward is about to overwrite
+    with NaN; if any element were not rewritten the update would turn non-finite. The
+    results must equal the normal mode bitwise."""
+    def run():
+        c, m = _model()
+        opt = N.AdamW(m.sharding, lr=1e-3, lazy_zero=True)
+        out = []
+        for _ in range(3):
+            r = _step(c, m, opt)
+            out.append((float(r.metrics.loss), bool(r.update["updated"]), r.update["grad_norm"]))
+        return out, [s.master.clone() for s in m.sharding]
+    monkeypatch.setenv("NANOSPEC_DEBUG", "0")
+    ref, ref_m = run()
+    monkeypatch.setenv("NANOSPEC_DEBUG", "1")
+    got, got_m = run()
+    assert got == ref and all(u for _, u, _ in got)
+    for a, b in zip(ref_m, got_m):
+        assert torch.equal(a, b)
