@@ -47,6 +47,17 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// acc[0..1] += f * v[0..1] with one paired fp32 FMA (fma.rn.f32x2, sm_100): half the
+// issue slots of the promotion's scalar FMAs.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float f, float v0, float v1) {
+  uint64_t acc, vv, ff;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(vv) : "f"(v0), "f"(v1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ff) : "f"(f));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(ff), "l"(vv));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+}
+
 struct F8Args {
   int M, N, K;
   const float* sa;  // [M, K/128]
@@ -182,7 +193,7 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
           float v[32];
           sm100::tmem_ld32(tmem + lane_off + (uint32_t)(buf * BN + seg * CPW + c), v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c + j] = fmaf(f, v[j], acc[c + j]);
+          for (int j = 0; j < 32; j += 2) ffma2(acc[c + j], acc[c + j + 1], f, v[j], v[j + 1]);
         }
         sm100::tc_fence_before();
         sm100::mbar_arrive(&tempty[buf]);
