@@ -57,6 +57,11 @@ void peer_reduce_avg_ce(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tens
 void peer_allgather_ce(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out);
 void peer_allgather(int64_t id, int64_t src_off, int64_t ss_elems, at::Tensor out);
 void peer_reduce_avg(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad);
+void peer_reduce_local(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad);
+void ag_gemm(int64_t id, int64_t src_off, int64_t ss, at::Tensor resident, int64_t w_off, int64_t N, int64_t K,
+             at::Tensor x, at::Tensor out, at::Tensor flags, at::Tensor claim, int64_t epoch, int64_t poll_limit);
+void gemm_rs(int64_t id, int64_t slot_off, int64_t ss, int64_t g_off, at::Tensor dy, at::Tensor x);
+void peer_push(int64_t id, int64_t slot_off, int64_t ss, at::Tensor src, int64_t lo, int64_t hi);
 void peer_signal(int64_t id, int64_t flags_off, int64_t channel, int64_t seq);
 void peer_wait(int64_t id, int64_t flags_off, int64_t channel, int64_t seq, int64_t poll_limit);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
@@ -122,6 +127,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_allgather_ce", &ns::peer_allgather_ce);
   m.def("peer_allgather", &ns::peer_allgather);
   m.def("peer_reduce_avg", &ns::peer_reduce_avg);
+  m.def("peer_reduce_local", &ns::peer_reduce_local);
+  m.def("ag_gemm", &ns::ag_gemm);
+  m.def("gemm_rs", &ns::gemm_rs);
+  m.def("peer_push", &ns::peer_push);
   m.def("peer_signal", &ns::peer_signal);
   m.def("peer_wait", &ns::peer_wait);
   m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);

@@ -18,15 +18,10 @@
 #include <vector>
 
 #include "common.h"
+#include "peer.h"
 #include "sm100.cuh"
 
 namespace ns {
-
-constexpr int MAX_PEERS = 8;
-
-struct PeerTable {
-  uint64_t base[MAX_PEERS];  // window base address of each rank, as seen from this rank
-};
 
 // ---------------------------------------------------------------------------- flags
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -244,6 +239,12 @@ void window_close(int64_t id) {
   g_windows[id] = nullptr;
 }
 
+WindowInfo window_info(int64_t id) {
+  NS_CHECK(id >= 0 && id < (int64_t)g_windows.size() && g_windows[id], "peer window is not open");
+  const Window* w = g_windows[id];
+  return {w->table, w->rank, w->world, w->bytes};
+}
+
 // A tensor view of this rank's window (bytes [offset, offset + numel*itemsize)).
 at::Tensor window_view(int64_t id, int64_t offset, int64_t numel, at::ScalarType dtype) {
   Window* w = g_windows.at(id);
@@ -325,6 +326,21 @@ void peer_reduce_avg_ce(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tens
   local_reduce_avg_kernel<<<blocks, 256, 0, stream()>>>(own, reinterpret_cast<const __nv_bfloat16*>(st), w->world,
                                                         w->rank, ss_elems,
                                                         reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
+  NS_CUDA(cudaGetLastError());
+}
+
+// Reduce after pushes: every rank stored its contribution to this rank's shard into
+// row p (p = its rank) of this rank's slot ([world][ss] bf16, local memory), so the
+// sum reads only local memory, in the same rank order and rounding as the pull paths.
+void peer_reduce_local(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tensor grad) {
+  Window* w = g_windows.at(id);
+  NS_CHECK(slot_off % 16 == 0 && ss_elems % 8 == 0 && reinterpret_cast<uintptr_t>(grad.data_ptr()) % 16 == 0,
+           "push-mode reduce needs 16-byte aligned shards");
+  NS_CHECK(grad.numel() >= ss_elems, "gradient shard too small");
+  const auto* slot = reinterpret_cast<const __nv_bfloat16*>(w->table.base[w->rank] + slot_off);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((ss_elems / 8 + 255) / 256, (int64_t)num_sms() * 2));
+  local_reduce_avg_kernel<<<blocks, 256, 0, stream()>>>(slot + (int64_t)w->rank * ss_elems, slot, w->world, w->rank,
+                                                        ss_elems, reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
   NS_CUDA(cudaGetLastError());
 }
 

@@ -51,10 +51,23 @@ def _cat_rows(a, b):
 class _Grads:
     """Gradient views of one unit, bound for the duration of its backward."""
 
-    def __init__(self, unit, buffer):
+    def __init__(self, unit, buffer, sched=None, index=None):
         self.unit = unit
         self.flat = buffer
         self.views = unit.views(buffer)
+        self.sched = sched
+        self.index = index
+
+    def wgrad(self, dy, x, first, last=None, norm=None):
+        """``dW = dy^T x`` for parameter ``first`` (or the adjacent span ``first ..
+        last``). A schedule that reduce-scatters by pushes takes it into its fused
+        weight-gradient GEMM (the epilogue stores into the owners' slots); otherwise
+        the GEMM writes the gradient view."""
+        out = self.span(first, last) if last is not None else self.views[first]
+        push = getattr(self.sched, "push_wgrad", None)
+        if norm is None and push is not None and push(self.index, dy, x, self.unit.offsets[first][0], out.shape):
+            return
+        ops.linear_wgrad(dy, x, out, norm=norm)
 
     def __getitem__(self, name):
         return self.views[name]
@@ -92,7 +105,7 @@ def _bind_grads(sched, index, unit):
             buf[unit.numel:].zero_()
     unit.full_grad = buf
     unit.bind_gradients(buf)
-    return _Grads(unit, buf)
+    return _Grads(unit, buf, sched, index)
 
 
 def _reduce(sched, index, unit):
@@ -140,21 +153,29 @@ class DraftStep:
         feats = [h.to(dtype) for h in teacher.hidden_states]
 
         # ---------------------------------------------------------- context unit
-        sched.prefetch(0)
-        sched.acquire(0)
-        sched.prefetch(1)
         fc_saved = []
-        if m.fc_norm:
-            normed = []
-            for norm, f in zip(m.fc_norm, feats):
-                y, inv = ops.rms_norm(f, norm.weight, norm.eps)
-                normed.append(y)
-                fc_saved.append(inv)
-            context_input = torch.cat(normed, -1)
+        fused_first = not m.fc_norm and hasattr(sched, "acquire_linear")
+        if fused_first:
+            # the projection is the unit's first consumer: a peer schedule may gather
+            # the unit inside this GEMM
+            context_input = torch.cat(feats, -1).reshape(b * s, -1)
+            projected = sched.acquire_linear(0, context_input, "context_proj.weight")
+            sched.prefetch(1)
         else:
-            context_input = torch.cat(feats, -1)
-        context_input = context_input.reshape(b * s, -1)
-        projected = ops.linear(context_input, m.context_proj.weight)
+            sched.prefetch(0)
+            sched.acquire(0)
+            sched.prefetch(1)
+            if m.fc_norm:
+                normed = []
+                for norm, f in zip(m.fc_norm, feats):
+                    y, inv = ops.rms_norm(f, norm.weight, norm.eps)
+                    normed.append(y)
+                    fc_saved.append(inv)
+                context_input = torch.cat(normed, -1)
+            else:
+                context_input = torch.cat(feats, -1)
+            context_input = context_input.reshape(b * s, -1)
+            projected = ops.linear(context_input, m.context_proj.weight)
         context, inv_ctx = ops.rms_norm(projected, m.context_norm.weight, m.context_norm.eps)
         sched.release(0)
 
@@ -250,17 +271,17 @@ class DraftStep:
             sv = saved.pop()
             attn, mlp = layer.self_attn, layer.mlp
             dp = ops.linear_dgrad(dx, mlp.down_proj.weight)
-            ops.linear_wgrad(dx, sv["prod"], g["mlp.down_proj.weight"], norm=nrm)
+            g.wgrad(dx, sv["prod"], "mlp.down_proj.weight", norm=nrm)
             dgu = ops.swiglu_backward(dp, sv["gu"])
             del dp
             dn2 = ops.linear_dgrad(dgu, _span(unit, "mlp.gate_proj.weight", "mlp.up_proj.weight"))
-            ops.linear_wgrad(dgu, sv["n2"], g.span("mlp.gate_proj.weight", "mlp.up_proj.weight"), norm=nrm)
+            g.wgrad(dgu, sv["n2"], "mlp.gate_proj.weight", "mlp.up_proj.weight", norm=nrm)
             del dgu
             dr = ops.rms_norm_backward(dn2, sv["x1"], sv["inv_2"], layer.post_attention_layernorm.weight,
                                        g["post_attention_layernorm.weight"], residual=dx)
             del dn2
             da = ops.linear_dgrad(dr, attn.o_proj.weight)
-            ops.linear_wgrad(dr, sv["a_out"].reshape(b * td, qd), g["self_attn.o_proj.weight"], norm=nrm)
+            g.wgrad(dr, sv["a_out"].reshape(b * td, qd), "self_attn.o_proj.weight", norm=nrm)
             dkv = torch.empty_like(sv["kv"])
             dk_rot = torch.empty(b * (s + td), hk, d, device=x.device, dtype=dtype)
             dq_rot, _, _ = ops.attention_backward(
@@ -278,14 +299,13 @@ class DraftStep:
             del dq_rot, dk_rot
             wkv = _span(unit, "self_attn.k_proj.weight", "self_attn.v_proj.weight")
             dxin = ops.linear_dgrad(dkv, wkv)
-            ops.linear_wgrad(dkv, sv["xin"], g.span("self_attn.k_proj.weight", "self_attn.v_proj.weight"),
-                              norm=nrm)
+            g.wgrad(dkv, sv["xin"], "self_attn.k_proj.weight", "self_attn.v_proj.weight", norm=nrm)
             del dkv
             dq2 = dq.reshape(b * td, qd)
             n = sv["xin"][b * s:]
             dn = dxin[b * s:]
             ops.linear_dgrad(dq2, attn.q_proj.weight, out=dn, accumulate=True)
-            ops.linear_wgrad(dq2, n, g["self_attn.q_proj.weight"], norm=nrm)
+            g.wgrad(dq2, n, "self_attn.q_proj.weight", norm=nrm)
             del dq, dq2
             dx = ops.rms_norm_backward(dn, sv["x"], sv["inv_in"], layer.input_layernorm.weight,
                                        g["input_layernorm.weight"], residual=dr)
@@ -299,8 +319,8 @@ class DraftStep:
         g = _bind_grads(sched, visit, unit)
         dproj = ops.rms_norm_backward(dc, projected, inv_ctx, m.context_norm.weight,
                                       g["context_norm.weight"])
-        ops.linear_wgrad(dproj, context_input, g["context_proj.weight"],
-                          norm=self.norm.bind(unit) if self.norm is not None else None)
+        g.wgrad(dproj, context_input, "context_proj.weight",
+                norm=self.norm.bind(unit) if self.norm is not None else None)
         if m.fc_norm:
             dcat = ops.linear_dgrad(dproj, m.context_proj.weight)
             width = c.target_hidden_size

@@ -15,6 +15,14 @@ full-size gradient slots and a flag area; peers address it at the same offsets.
   shard-range of every peer's slot (copy-engine DMA into a staging buffer, or an SM
   kernel), sums the N contributions in fixed rank order, averages and adds into its
   gradient shard (deterministic, NCCL AVG semantics);
+* fused variants (``NANOSPEC_PEER_GATHER=fused``, ``NANOSPEC_PEER_REDUCE=push``):
+  the context unit is gathered by the first GEMM that consumes it (``ag_gemm``:
+  puller warps inside the GEMM fetch the unit's chunks and the tensor-core tiles
+  start on each W tile as soon as its chunks are in), and every weight-gradient
+  GEMM stores its bf16 output straight into the owners' window slots from its
+  epilogue (``gemm_rs``); the remaining small gradients are pushed by a copy
+  kernel, and each owner sums the rows of its own slot in rank order. Values are
+  the same as the pull paths';
 * synchronisation is by sequence-number flags in the windows (release stores /
   acquire loads) with bounded waits: a peer that never signals makes the wait
   kernel set the device error word and return, and the host raises.
@@ -49,6 +57,11 @@ CH_UNIT = 8  # CH_UNIT + i: "unit i's parameters are final" (published per unit 
 
 def _align(n, a=256):
     return (n + a - 1) // a * a
+
+
+def _weight(unit, name):
+    lo, hi = unit.offsets[name]
+    return unit.gathered[lo:hi].view(unit.shapes[name])
 
 
 class PeerWindow:
@@ -116,6 +129,28 @@ class PeerSchedule:
         # Reduce-scatter: "ce" DMAs the peers' slot ranges into `staging` and sums
         # locally; "sm" pulls and sums in one SM kernel. Same values either way.
         self.reduce_engine = os.environ.get("NANOSPEC_PEER_REDUCE", "ce")
+        # The fused paths address 8-element (16-byte) vectors of the flat unit.
+        aligned = all(u.shard_size % 8 == 0 for u in units)
+        if self.reduce_engine == "push" and not aligned:
+            self.reduce_engine = "ce"
+        if self.gather_engine == "fused" and not aligned:
+            self.gather_engine = "ce"
+        self.push = self.reduce_engine == "push"
+        self.local_grad = None
+        self.pushed = [[], []]
+        if self.push:
+            # small gradients (norms, embeddings) are written here, then pushed
+            size = max(u.full_size for u in units)
+            self.local_grad = [torch.empty(size, device=self.device, dtype=units[0].param.dtype) for _ in range(2)]
+        # fused gather: the first unit (the context projection) is gathered by its GEMM
+        self.fused_keys = {id(units[0])} if self.gather_engine == "fused" else set()
+        if self.fused_keys:
+            chunk = min(16384, units[0].shard_size)
+            self.ag_flags = torch.zeros((units[0].full_size + chunk - 1) // chunk, device=self.device,
+                                        dtype=torch.int32)
+            self.ag_claim = torch.zeros(1, device=self.device, dtype=torch.int32)
+            self.ag_epoch = 0
+        self.params_final = torch.cuda.Event()
         self.staging = None
         if self.reduce_engine == "ce":
             self.staging = torch.empty(self.w.world * max(u.shard_size for u in units), device=self.device,
@@ -152,13 +187,15 @@ class PeerSchedule:
         with torch.cuda.stream(self.stream):
             self._signal(CH_PARAMS)
             self._wait(CH_PARAMS, self.seq[CH_PARAMS])  # every peer's shards are final
+            self.params_final.record(self.stream)
         self.gathered, self.pregathered = self.pregathered, set()
         self.active = True
         if not self.serial:
             # Gather every unit now, back to back, in visit order: the link never idles
             # waiting for compute, and compute waits only for the unit it needs.
             for i in range(len(visits)):
-                self.prefetch(i)
+                if id(visits[i]) not in self.fused_keys:
+                    self.prefetch(i)
 
     def prefetch(self, index):
         if index >= len(self.visits):
@@ -180,6 +217,8 @@ class PeerSchedule:
         if self.active:
             return  # an update inside a step: the next ``begin`` gathers as usual
         key = id(unit)
+        if key in self.fused_keys:
+            return  # gathered by its first GEMM in the next step
         ch = CH_UNIT + self.unit_index[key]
         self.seq.setdefault(ch, 0)
         self._signal(ch)
@@ -201,6 +240,50 @@ class PeerSchedule:
         unit.bind(unit.gathered)
         return unit
 
+    def acquire_linear(self, index, x, name):
+        """Acquire unit ``index`` and return ``x @ W^T`` for its parameter ``name``.
+
+        In the fused gather mode the unit is gathered by that GEMM (``ag_gemm``):
+        the GEMM waits only for the chunks of W each tile reads, and the whole unit
+        is resident when it finishes. Otherwise: gather, acquire, plain GEMM."""
+        from .. import ops
+        unit = self.visits[index]
+        key = id(unit)
+        lo, hi = unit.offsets[name]
+        shape = unit.shapes[name]
+        if key not in self.fused_keys or key in self.gathered or lo % 8:
+            self.prefetch(index)
+            self.acquire(index)
+            return ops.linear(x, _weight(unit, name))
+        if unit.gathered is not None:
+            raise ScheduleError("Acquire exactly one prefetched unit")
+        self.gathered.add(key)
+        x2 = x.reshape(-1, x.shape[-1])
+        out = torch.empty(x2.shape[0], shape[0], device=x.device, dtype=x.dtype)
+        self.compute.wait_event(self.params_final)
+        self.ag_epoch += 1
+        self.C.ag_gemm(self.w.id, self.w.param_off[key], unit.shard_size, self.resident[key], lo, shape[0],
+                       shape[1], x2, out, self.ag_flags, self.ag_claim, self.ag_epoch, self.poll_limit)
+        self.ready[key].record(self.compute)
+        unit.gathered = self.resident[key]
+        unit.bind(unit.gathered)
+        return out.view(*x.shape[:-1], shape[0])
+
+    def push_wgrad(self, index, dy, x, offset, shape):
+        """Push mode: ``dW = dy^T x`` for the tensor at element ``offset`` of unit
+        ``index``, stored by the GEMM's epilogue into the owners' slots. Returns
+        False when this schedule does not push (the caller writes the view)."""
+        if not self.push or offset % 8 or shape[-1] % 8:
+            return False
+        unit = self.visits[index]
+        slot = index % 2
+        if self.slot_owner[slot] != index:
+            raise ScheduleError("push without a bound gradient slot")
+        dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
+        self.C.gemm_rs(self.w.id, self.w.slot_off[slot], unit.shard_size, offset, dy2, x2)
+        self.pushed[slot].append((offset, offset + shape[0] * shape[1]))
+        return True
+
     def gradient_buffer(self, index):
         unit = self.visits[index]
         slot = index % 2
@@ -209,9 +292,11 @@ class PeerSchedule:
         # Every peer must have pulled this slot's previous contents.
         self._wait(CH_PULLED + slot, self.seq[CH_PULLED + slot])
         self.slot_owner[slot] = index
+        buf = (self.local_grad[slot] if self.push else self.w.slots[slot])[:unit.full_size]
+        self.pushed[slot] = []
         if _debug.enabled():  # every element must be rewritten by this unit's backward
-            _debug.poison(self.w.slots[slot][:unit.full_size])
-        return self.w.slots[slot][:unit.full_size]
+            _debug.poison(buf)
+        return buf
 
     def release(self, index):
         unit = self.visits[index]
@@ -225,12 +310,22 @@ class PeerSchedule:
         self.slot_owner[slot] = None
         unit.full_grad = None
         self.release(index)
+        if self.push:
+            # the gradients no GEMM pushed: the gaps between the pushed ranges
+            at = 0
+            for lo, hi in sorted(self.pushed[slot]) + [(unit.full_size, unit.full_size)]:
+                if lo > at:
+                    self.C.peer_push(self.w.id, self.w.slot_off[slot], unit.shard_size, self.local_grad[slot], at, lo)
+                at = max(at, hi)
+            self.pushed[slot] = []
         self._signal(CH_READY + slot)  # on compute: my slot holds unit's full gradient
         seq = self.seq[CH_READY + slot]
         self.stream.wait_stream(self.compute)
         with torch.cuda.stream(self.stream):
             self._wait(CH_READY + slot, seq)
-            if self.staging is not None:
+            if self.push:
+                self.C.peer_reduce_local(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad)
+            elif self.staging is not None:
                 self.C.peer_reduce_avg_ce(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad, self.staging)
             else:
                 self.C.peer_reduce_avg(self.w.id, self.w.slot_off[slot], unit.shard_size, unit.grad)

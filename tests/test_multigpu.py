@@ -158,3 +158,142 @@ def test_peer_wait_times_out_without_hanging():
     x = torch.ones(4, device="cuda")
     assert (x + 1).sum().item() == 8
     C.window_close(wid)
+
+
+def _open_window(C, rank, world, nbytes):
+    wid, _ = C.window_create(nbytes, rank, world)
+    handles = [None] * world
+    dist.all_gather_object(handles, C.window_ipc_handle(wid).tolist())
+    C.window_open(wid, torch.tensor(handles, dtype=torch.uint8))
+    return wid
+
+
+def _fused_kernels(rank, world):
+    """ag_gemm gathers the whole unit and multiplies by its W; gemm_rs + peer_push +
+    peer_reduce_local produce the averaged gradient shard of every rank."""
+    from nanospec_b200.ops._ext import cuda_ops
+    C = cuda_ops()
+    dev = torch.device("cuda", rank)
+    Nw, K, M, T, pre, post = 384, 512, 300, 200, 1000, 2000
+    total = pre + Nw * K + post
+    ss = -(-total // (8 * world)) * 8
+    full_n = ss * world
+    g = torch.Generator(device=dev).manual_seed(1)
+    unit = (torch.randn(full_n, device=dev, generator=g) * 0.05).bfloat16()
+    param_off, slot_off = 4096, 4096 + ((ss * 2 + 255) // 256) * 256
+    wid = _open_window(C, rank, world, slot_off + full_n * 2)
+    C.window_view(wid, param_off, ss, torch.bfloat16).copy_(unit[rank * ss:(rank + 1) * ss])
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    # ---- all-gather -> GEMM, twice (the flags advance by epoch)
+    W = unit[pre:pre + Nw * K].view(Nw, K)
+    x = (torch.randn(M, K, device=dev, generator=g) * 0.5).bfloat16()
+    flags = torch.zeros(-(-full_n // min(16384, ss)), device=dev, dtype=torch.int32)
+    claim = torch.zeros(1, device=dev, dtype=torch.int32)
+    ref = x.float() @ W.float().t()
+    for epoch in (1, 2):
+        resident = torch.full((full_n,), float("nan"), device=dev, dtype=torch.bfloat16)
+        out = torch.empty(M, Nw, device=dev, dtype=torch.bfloat16)
+        C.ag_gemm(wid, param_off, ss, resident, pre, Nw, K, x, out, flags, claim, epoch, 50_000_000)
+        torch.cuda.synchronize()
+        assert C.device_error() == 0
+        assert torch.equal(resident, unit), "the gathered unit must equal every rank's shards"
+        err = (out.float() - ref).abs().max().item()
+        assert err <= 2e-2 * ref.abs().max().item(), err
+
+    # ---- weight-gradient GEMM -> reduce-scatter (push), then the local sum
+    gr = torch.Generator(device=dev).manual_seed(50 + rank)
+    dy = (torch.randn(T, Nw, device=dev, generator=gr) * 0.5).bfloat16()
+    xx = (torch.randn(T, K, device=dev, generator=gr) * 0.5).bfloat16()
+    local = (torch.randn(full_n, device=dev, generator=gr) * 0.01).bfloat16()  # this rank's small grads
+    C.gemm_rs(wid, slot_off, ss, pre, dy, xx)
+    C.peer_push(wid, slot_off, ss, local, 0, pre)
+    C.peer_push(wid, slot_off, ss, local, pre + Nw * K, full_n)
+    C.peer_signal(wid, 0, 4, 1)
+    C.peer_wait(wid, 0, 4, 1, 50_000_000)
+    grad = torch.zeros(ss, device=dev, dtype=torch.bfloat16)
+    C.peer_reduce_local(wid, slot_off, ss, grad)
+    torch.cuda.synchronize()
+    assert C.device_error() == 0
+    # every rank's full contribution, to build the expected shard on the host
+    mine = local.clone()
+    mine[pre:pre + Nw * K] = (dy.float().t() @ xx.float()).bfloat16().reshape(-1)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    acc = parts[0][rank * ss:(rank + 1) * ss].float()
+    for q in range(1, world):
+        acc = acc + parts[q][rank * ss:(rank + 1) * ss].float()
+    want = (acc * (1.0 / world)).bfloat16().float()
+    lo, hi = max(pre - rank * ss, 0), min(pre + Nw * K - rank * ss, ss)
+    outside = torch.ones(ss, dtype=torch.bool, device=dev)
+    if hi > lo:
+        outside[lo:hi] = False
+    # pushed copies are exact; GEMM outputs may differ from torch's fp32 GEMM by an ulp
+    assert torch.equal(grad.float()[outside], want[outside])
+    if hi > lo:
+        d = (grad.float()[lo:hi] - want[lo:hi]).abs().max().item()
+        assert d <= 2e-2 * want[lo:hi].abs().max().item(), d
+    torch.cuda.synchronize()
+    dist.barrier()
+    C.window_close(wid)
+
+
+def _fused_schedules(rank, world):
+    """The fused paths (gather inside the context GEMM, reduce-scatter from the
+    weight-gradient epilogues): serial and overlapped are bitwise equal, and they
+    match the NCCL schedule as closely as the pull-based peer schedule does."""
+    os.environ["NANOSPEC_PEER_GATHER"] = "fused"
+    os.environ["NANOSPEC_PEER_REDUCE"] = "push"
+    c, m = _model(rank, world)
+    o = N.Objective(num_anchors=8)
+    ids, hs, last, mask = _data(c, rank)
+    init = [s.param.clone() for s in m.sharding]
+    results = {}
+    for mode in ("nccl_serial", "peer_serial", "peer_overlap"):
+        if mode.startswith("peer"):
+            m.sharding.enable_peer()
+            sched = m.sharding._cache["peer"]
+            assert sched.push and sched.fused_keys, "fused paths not selected"
+        for s, p0 in zip(m.sharding, init):
+            s.param.copy_(p0)
+            s.master.copy_(s.param)
+            s.m.zero_(), s.v.zero_(), s.grad.zero_()
+        m.sharding.parameters_changed()
+        opt = N.AdamW(m.sharding, lr=1e-3, weight_decay=0.01)
+        rows = []
+        for _ in range(3):
+            torch.manual_seed(7 + rank)
+            r = N.train(ids, m, o, teacher_batch=N.TeacherBatch(hs, last), loss_mask=mask, optimizer=opt,
+                        overlap=mode.endswith("overlap"))
+            rows.append((r.metrics.loss.item(), r.update["grad_norm"], r.hidden.clone()))
+        results[mode] = (rows, _digest(m))
+    from nanospec_b200.ops._ext import cuda_ops
+    assert cuda_ops().device_error() == 0
+    m.sharding.close_peer()
+    a, b = results["peer_serial"], results["peer_overlap"]
+    for ra, rb in zip(a[0], b[0]):
+        assert ra[0] == rb[0] and ra[1] == rb[1] and torch.equal(ra[2], rb[2])
+    for x, y in zip(a[1], b[1]):
+        assert torch.equal(x, y), "fused serial vs overlap must be bitwise equal"
+    for ra, rb in zip(results["nccl_serial"][0], results["peer_serial"][0]):
+        assert abs(ra[0] - rb[0]) <= 1e-3 * abs(ra[0])
+    tol = 1.5e-3 * world
+    for x, y in zip(results["nccl_serial"][1], results["peer_serial"][1]):
+        rel = ((x.float() - y.float()).norm() / x.float().norm().clamp_min(1e-12)).item()
+        assert rel < tol, rel
+
+
+@two_gpus
+def test_fused_allgather_gemm_and_gemm_reduce_scatter_kernels():
+    run_ranks(2, _fused_kernels)
+
+
+@two_gpus
+def test_fused_schedules_bitwise_and_match_nccl():
+    run_ranks(2, _fused_schedules)
+
+
+@pytest.mark.skipif(ngpu < 4, reason="needs 4 GPUs")
+def test_fused_kernels_four_ranks():
+    run_ranks(4, _fused_kernels)
