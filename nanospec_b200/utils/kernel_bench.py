@@ -316,10 +316,54 @@ def bench_gemm_suite(a):
             "total_cublas_us": round(sum(r["cublas_us"] for r in rows), 1)}
 
 
+def bench_fused(a):
+    """The fused collective GEMMs on ONE GPU: a window of world 1, so every "peer"
+    access is local. Measures the kernels' own efficiency (no NVLink) against the
+    plain GEMMs of the same shape: x [T, k] · W [nout, k]^T and dy^T · x."""
+    from nanospec_b200 import ops
+    from nanospec_b200.ops._ext import cuda_ops
+    C = cuda_ops()
+    dev = torch.device("cuda")
+    T, N, K = a.T, a.nout, a.k
+    ss = -(-N * K // 8) * 8
+    wid, _ = C.window_create(4096 + 2 * ss * 2 + 4096, 0, 1)
+    C.window_open(wid, C.window_ipc_handle(wid).view(1, -1))
+    param_off, slot_off = 4096, 4096 + ((ss * 2 + 4095) // 4096) * 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    C.window_view(wid, param_off, ss, torch.bfloat16).copy_((torch.randn(ss, device=dev, generator=g) * 0.02).bfloat16())
+    x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+    dy = torch.randn(T, N, device=dev, generator=g).bfloat16()
+    resident = torch.empty(ss, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+    flags = torch.zeros(-(-ss // min(16384, ss)), device=dev, dtype=torch.int32)
+    claim = torch.zeros(1, device=dev, dtype=torch.int32)
+    ep = [0]
+
+    def ag():
+        ep[0] += 1
+        C.ag_gemm(wid, param_off, ss, resident, 0, N, K, x, out, flags, claim, ep[0], 200_000_000)
+
+    w = resident[:N * K].view(N, K)
+    dw = torch.empty(N, K, device=dev, dtype=torch.bfloat16)
+    flops = 2.0 * T * N * K
+    res = {"op": "fused", "T": T, "nout": N, "k": K}
+    for name, fn in (("ag_gemm", ag), ("linear", lambda: ops.linear(x, w)),
+                     ("gemm_rs", lambda: C.gemm_rs(wid, slot_off, ss, 0, dy, x)),
+                     ("linear_wgrad", lambda: ops.linear_wgrad(dy, x, dw)),
+                     ("torch_wgrad", lambda: torch.matmul(dy.t(), x))):
+        us = _time(fn, a.reps, a.warmup)
+        res[name + "_us"] = round(us, 1)
+        res[name + "_tflops"] = round(flops / us / 1e6, 1)
+    torch.cuda.synchronize()
+    assert C.device_error() == 0
+    C.window_close(wid)
+    return res
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn", "gemm-suite",
-                                     "verifier"))
+                                     "verifier", "fused"))
     p.add_argument("--kind", choices=("fwd", "dgrad", "wgrad"), default="fwd")
     p.add_argument("--T", type=int, default=56)
     p.add_argument("--nout", type=int, default=5120)
@@ -338,7 +382,7 @@ def main(argv=None):
     a = p.parse_args(argv)
     fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
           "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite,
-          "verifier": bench_verifier}[a.op]
+          "verifier": bench_verifier, "fused": bench_fused}[a.op]
     print(json.dumps(fn(a)), flush=True)
 
 
