@@ -1,10 +1,16 @@
 """CUDA path of the fused head: LM head + Markov head + CE/KL, vocabulary streamed.
 
-With the draft's few tokens the kernels (csrc/head.cu) hold the whole ``[2T, V]``
-logits in HBM (tens of MB) and stream each weight once per pass; for large T they
-fall back to ``[2T, chunk]`` slices. They return per-token statistics (CE, KL, sum_v min(p, q), the two log-sum-
-exps) and the gradients ``dh``/``de``/``dW2``; the weighted sums and the
-acceptance-length metric are formed here from those per-token values.
+The default kernels (``head_tc_kernel`` in csrc/head.cu) never write the logits:
+each 128-token x 128-vocabulary tile of the draft, Markov and target logits lives
+in TMEM, and the epilogue folds it into per-token online statistics (pass 1:
+log-sum-exps, the target-weighted gap, the label logit) or into the bf16 logits
+gradient of one vocabulary chunk (pass 2, followed by the dh / de / dW2 GEMMs on
+that chunk). They run whenever the logits would exceed 4 GiB; below that (the draft's few
+hundred tokens) the form that holds the ``[2T, V]`` logits in HBM is faster and is used
+(``NANOSPEC_HEAD=streamed | materialize`` overrides the choice). Both return per-token statistics (CE, KL,
+sum_v min(p, q), the two log-sum-exps) and the gradients ``dh``/``de``/``dW2``;
+the weighted sums and the acceptance-length metric are formed here from those
+per-token values. Reference: nanospec/objective.py:39-80, nanospec/train.py:269-311.
 """
 
 from __future__ import annotations
@@ -15,7 +21,9 @@ import torch
 
 from ._ext import cuda_ops
 
-# 0 = automatic: the whole vocabulary in one chunk while [3T, V] bf16 fits in 4 GiB.
+# Vocabulary columns per chunk; 0 = automatic. Streamed path: the whole vocabulary
+# while the [T, V] bf16 gradient fits in 1 GiB, else 512 MB gradient chunks.
+# Materialised path: the whole vocabulary while [R + T, V] bf16 fits in 4 GiB.
 VOCAB_CHUNK = int(os.environ.get("NANOSPEC_VOCAB_CHUNK", 0))
 
 

@@ -210,13 +210,17 @@ def test_attention(d, hq, hk, S, bs):
 
 
 @cuda
+@pytest.mark.parametrize("path", ["streamed", "materialize"])
 @pytest.mark.parametrize("markov,teacher_logits,chunk", [(True, False, 0), (False, False, 0), (True, True, 0),
                                                           (True, False, 4096), (True, True, 4096)])
-def test_head_loss(markov, teacher_logits, chunk, monkeypatch):
+def test_head_loss(markov, teacher_logits, chunk, path, monkeypatch):
+    """Both CUDA head paths against the fp32 statements: the streamed one (logits
+    only in TMEM, gradient per vocabulary chunk) and the materialised one."""
     import nanospec_b200 as N
     import nanospec_b200.ops.head as head_mod
     from nanospec_b200.objective import head_loss
     monkeypatch.setattr(head_mod, "VOCAB_CHUNK", chunk)  # 0: whole vocabulary; 4096: five chunks
+    monkeypatch.setenv("NANOSPEC_HEAD", path)
     torch.manual_seed(1)
     V, H, r = 20003, 256, 32  # V % 8 != 0: scalar tails and padded row strides
     b, nb, bs, S = 1, 8, 7, 64
