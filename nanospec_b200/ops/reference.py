@@ -326,6 +326,110 @@ def gated_delta_rule_chunked(q, k, v, g, beta, chunk=64):
     return out.to(dtype)
 
 
+def gated_delta_rule_backward_chunked(q, k, v, g, beta, dout, chunk=64):
+    """Gradients (dq, dk, dv, dg, dbeta) of the gated delta rule, chunked, explicit.
+
+    The statements that the chunked backward kernels (csrc/gdn_bwd.cu) implement;
+    fp32, no autograd. q, k [b, s, h, dk] raw (per value head), v/dout [b, s, h, dv],
+    g, beta [b, s, h]. Per chunk (in-chunk cumulative decay G, gam = e^G, Gam the
+    causal decay matrix, T = I + M with M = strict(beta k k^T * Gam)):
+      U = T^-1 (beta v), W = T^-1 (beta gam k), A = incl(q k^T * Gam),
+      Kh = e^{G_C - G} k, VN = U - W S0, O = gam q S0 + A VN, S1 = e^{G_C} S0 + Kh^T VN.
+    Both carried quantities obey one linear recurrence per chunk, F = e^{G_C} I - Kh^T W:
+      S1 = F S0 + Kh^T U  (forward),   dS0 = F^T dS1 + (gam q)^T dO - W^T A^T dO  (reverse);
+    every other term is chunk-local:
+      dVN = A^T dO + Kh dS1, dA = incl(dO VN^T), dW = -dVN S0^T, dU = dVN,
+      dBv = T^-T dU, dBk = T^-T dW, dM = strict(-(dBv U^T + dBk W^T)),
+    then the products' chain rules into q, k, v, beta and G, G into g by a reverse
+    cumulative sum, and the L2-normalisation chain rule into the raw q and k.
+    """
+    qf, kf = q.float(), k.float()
+    scale = q.shape[-1] ** -0.5
+    rq = torch.rsqrt((qf * qf).sum(-1, keepdim=True) + 1e-6)
+    rk = torch.rsqrt((kf * kf).sum(-1, keepdim=True) + 1e-6)
+    qn, kn = qf * rq, kf * rk
+    b, s, h, dk = k.shape
+    dv = v.shape[-1]
+    pad = (-s) % chunk
+    n = (s + pad) // chunk
+
+    def chunks(t):  # [b, s, h, ...] -> [b, h, n, C, ...]
+        t = torch.nn.functional.pad(t, (0, 0) * (t.dim() - 3) + (0, 0, 0, pad)) if pad else t
+        return t.reshape(b, n, chunk, h, *t.shape[3:]).movedim(3, 1)
+
+    Q, K = chunks(qn * scale), chunks(kn)
+    V, dO = chunks(v.float()), chunks(dout.float())
+    gc, bc = chunks(g.float().unsqueeze(-1))[..., 0], chunks(beta.float().unsqueeze(-1))[..., 0]
+    G = gc.cumsum(-1)
+    gam = G.exp()
+    incl = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril()
+    strict = incl.tril(-1)
+    zero = torch.zeros((), device=q.device)
+    Gam = torch.where(incl, (G.unsqueeze(-1) - G.unsqueeze(-2)).clamp(max=0).exp(), zero)
+    KK = K @ K.transpose(-1, -2)
+    M = torch.where(strict, bc.unsqueeze(-1) * KK * Gam, zero)
+    eye = torch.eye(chunk, device=q.device)
+    Tinv = torch.linalg.solve_triangular(eye + M, eye.expand_as(M), upper=False, unitriangular=True)
+    Bv, Bk = V * bc.unsqueeze(-1), K * (bc * gam).unsqueeze(-1)
+    U, W = Tinv @ Bv, Tinv @ Bk
+    A = torch.where(incl, (Q @ K.transpose(-1, -2)) * Gam, zero)
+    GC = G[..., -1:]
+    eK = (GC - G).exp()
+    Kh = K * eK.unsqueeze(-1)
+    gC = GC.exp().unsqueeze(-1)  # [b, h, n, 1, 1]
+    F = gC * torch.eye(dk, device=q.device) - Kh.transpose(-1, -2) @ W
+    # forward states entering each chunk, gradients of the states leaving each chunk
+    S0 = torch.zeros(b, h, n, dk, dv, device=q.device)
+    for i in range(n - 1):
+        S0[:, :, i + 1] = F[:, :, i] @ S0[:, :, i] + Kh[:, :, i].transpose(-1, -2) @ U[:, :, i]
+    Pc = (Q * gam.unsqueeze(-1)).transpose(-1, -2) @ dO - W.transpose(-1, -2) @ (A.transpose(-1, -2) @ dO)
+    dS1 = torch.zeros(b, h, n, dk, dv, device=q.device)
+    for i in range(n - 1, 0, -1):
+        dS1[:, :, i - 1] = F[:, :, i].transpose(-1, -2) @ dS1[:, :, i] + Pc[:, :, i]
+    # chunk-local adjoints
+    VN = U - W @ S0
+    dVN = A.transpose(-1, -2) @ dO + Kh @ dS1
+    dA = torch.where(incl, dO @ VN.transpose(-1, -2), zero)
+    dQg = dO @ S0.transpose(-1, -2)
+    dKh = VN @ dS1.transpose(-1, -2)
+    dW = -dVN @ S0.transpose(-1, -2)
+    dBv = Tinv.transpose(-1, -2) @ dVN
+    dBk = Tinv.transpose(-1, -2) @ dW
+    dM = torch.where(strict, -(dBv @ U.transpose(-1, -2) + dBk @ W.transpose(-1, -2)), zero)
+    dV = bc.unsqueeze(-1) * dBv
+    kdk = (dBk * K).sum(-1)
+    dB = (dBv * V).sum(-1) + gam * kdk
+    dK = (bc * gam).unsqueeze(-1) * dBk
+    dG = bc * gam * kdk
+    E = dM * Gam
+    dB = dB + (E * KK).sum(-1)
+    dK = dK + bc.unsqueeze(-1) * (E @ K) + E.transpose(-1, -2) @ (bc.unsqueeze(-1) * K)
+    MM = dM * M
+    dG = dG + MM.sum(-1) - MM.sum(-2)
+    Fq = dA * Gam
+    dQ = Fq @ K
+    dK = dK + Fq.transpose(-1, -2) @ Q
+    AA = dA * A
+    dG = dG + AA.sum(-1) - AA.sum(-2)
+    dQ = dQ + gam.unsqueeze(-1) * dQg
+    dG = dG + gam * (Q * dQg).sum(-1)
+    dK = dK + eK.unsqueeze(-1) * dKh
+    tk = eK * (K * dKh).sum(-1)
+    dGC = tk.sum(-1) + gC[..., 0, 0] * (S0 * dS1).sum((-1, -2))
+    dG = dG - tk
+    dG[..., -1] = dG[..., -1] + dGC
+    dg = dG.flip(-1).cumsum(-1).flip(-1)
+
+    def unchunk(t):  # [b, h, n, C, ...] -> [b, s, h, ...]
+        t = t.movedim(1, 3).reshape(b, n * chunk, h, *t.shape[4:])
+        return t[:, :s]
+
+    dqs, dkn = unchunk(dQ) * scale, unchunk(dK)
+    dq = rq * (dqs - qn * (qn * dqs).sum(-1, keepdim=True))
+    dk = rk * (dkn - kn * (kn * dkn).sum(-1, keepdim=True))
+    return dq, dk, unchunk(dV), unchunk(dg.unsqueeze(-1))[..., 0], unchunk(dB.unsqueeze(-1))[..., 0]
+
+
 def causal_attention(q, k, v):
     """Verifier attention: q [b, s, Hq, D], k/v [b, s, Hk, D]; bf16 scores + fp32 softmax."""
     g = q.shape[2] // k.shape[2]
