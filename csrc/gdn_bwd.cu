@@ -1,4 +1,7 @@
 // Backward of the gated delta rule (the reference has none: its verifier is frozen).
+// Head dims 64 and 128 run the chunked kernels of gdn_bwd_chunk.cu; this file holds
+// the token-serial kernels (head dims 16 and 32, or NANOSPEC_GDN_BWD=serial) and the
+// per-key-head sum of dq / dk shared by both.
 //
 // Forward recurrence per (batch row, value head), state S [Dk x Dv] in fp32, with
 // kn = k / sqrt(|k|^2 + 1e-6), qs = q / sqrt(|q|^2 + 1e-6) * Dk^-1/2:
@@ -17,6 +20,8 @@
 //                     the chunk's 64 token states into a per-CTA scratch, then walks
 //                     the chunk backwards with S_t and dS in shared memory.
 //   gdn_group_sum   : sums dq/dk over the value heads sharing a key head (fixed order).
+#include <cstdlib>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -281,6 +286,9 @@ static void gdn_bwd_launch(GdnArgs a, int b) {
 
 // q, k [b, s, nk, D]; v, dout [b, s, nv, D]; g fp32 [b, s, nv]; beta [b, s, nv].
 // Returns dq, dk [b, s, nk, D] bf16; dv [b, s, nv, D] bf16; dg, dbeta [b, s, nv] fp32.
+bool gdn_bwd_chunked(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta, at::Tensor dout,
+                     int64_t groups, at::Tensor dq32, at::Tensor dk32, at::Tensor dv, at::Tensor dg, at::Tensor dbeta);
+
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
                                       at::Tensor dout, int64_t groups) {
   NS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && g.is_contiguous() && beta.is_contiguous() &&
@@ -290,13 +298,29 @@ std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, 
   NS_CHECK(v.size(3) == D && nv == nk * groups, "gdn_chunk_bwd: d_k == d_v and nv == nk * groups expected");
   const int nchunks = (s + GC - 1) / GC;
   auto f32 = q.options().dtype(at::kFloat);
-  auto ckpt = at::empty({(int64_t)b * nv * nchunks * D * D}, f32);
-  auto scratch = at::empty({(int64_t)b * nv * GC * D * D}, f32);
   auto dq32 = at::empty({b, s, nv, D}, f32);
   auto dk32 = at::empty({b, s, nv, D}, f32);
   auto dv = at::empty({b, s, nv, D}, q.options());
   auto dg = at::empty({b, s, nv}, f32);
   auto dbeta = at::empty({b, s, nv}, f32);
+  // head dims 64 / 128: the chunked kernels; NANOSPEC_GDN_BWD=serial keeps the
+  // token-serial ones (the only path for 16 / 32)
+  const char* mode = std::getenv("NANOSPEC_GDN_BWD");
+  const bool serial = mode && std::string(mode) == "serial";
+  if (!serial && gdn_bwd_chunked(q, k, v, g, beta, dout, groups, dq32, dk32, dv, dg, dbeta)) {
+    auto dq = at::empty({b, s, nk, D}, q.options());
+    auto dk = at::empty({b, s, nk, D}, q.options());
+    const int64_t tot = (int64_t)b * s * nk * D;
+    const int blocks = (int)std::min<int64_t>((tot + 255) / 256, (int64_t)num_sms() * 8);
+    gdn_group_sum_kernel<<<blocks, 256, 0, stream()>>>(dq32.data_ptr<float>(), reinterpret_cast<bf16*>(dq.data_ptr()),
+                                                       (int64_t)b * s, nk, (int)groups, D);
+    gdn_group_sum_kernel<<<blocks, 256, 0, stream()>>>(dk32.data_ptr<float>(), reinterpret_cast<bf16*>(dk.data_ptr()),
+                                                       (int64_t)b * s, nk, (int)groups, D);
+    NS_CUDA(cudaGetLastError());
+    return {dq, dk, dv, dg, dbeta};
+  }
+  auto ckpt = at::empty({(int64_t)b * nv * nchunks * D * D}, f32);
+  auto scratch = at::empty({(int64_t)b * nv * GC * D * D}, f32);
   GdnArgs a{};
   a.q = reinterpret_cast<const bf16*>(q.data_ptr());
   a.k = reinterpret_cast<const bf16*>(k.data_ptr());

@@ -115,8 +115,10 @@ def test_stage_forward_matches_cpu(tmp_path):
 
 
 @cuda
-@pytest.mark.parametrize("D,s,groups", [(16, 70, 2), (128, 130, 3)])
+@pytest.mark.parametrize("D,s,groups", [(16, 70, 2), (64, 200, 1), (128, 130, 3), (128, 64, 1)])
 def test_gated_delta_rule_backward(D, s, groups):
+    """Head dims 64 / 128 run the chunked kernels, 16 the token-serial ones; both
+    against autograd through the fp32 token recurrence."""
     b, nk = 1, 2
     nv = nk * groups
     q = torch.randn(b, s, nk, D).bfloat16()
@@ -129,6 +131,25 @@ def test_gated_delta_rule_backward(D, s, groups):
     got = vops.gated_delta_rule_backward(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), dout.cuda(), groups)
     for name, x, y in zip(("dq", "dk", "dv", "dg", "dbeta"), got, expect):
         close(x, y, rtol=3e-2, cos_min=0.999)
+
+
+@cuda
+def test_chunked_and_serial_gdn_backward_agree(monkeypatch):
+    """The chunked kernels and the token-serial kernels give the same gradients."""
+    torch.manual_seed(5)
+    b, s, nk, groups, D = 2, 300, 2, 2, 128
+    nv = nk * groups
+    q = torch.randn(b, s, nk, D).bfloat16().cuda()
+    k = torch.randn(b, s, nk, D).bfloat16().cuda()
+    v = torch.randn(b, s, nv, D).bfloat16().cuda()
+    g = (-torch.rand(b, s, nv) * 0.5).cuda()
+    beta = torch.rand(b, s, nv).bfloat16().cuda()
+    dout = torch.randn(b, s, nv, D).bfloat16().cuda()
+    chunked = vops.gated_delta_rule_backward(q, k, v, g, beta, dout, groups)
+    monkeypatch.setenv("NANOSPEC_GDN_BWD", "serial")
+    serial = vops.gated_delta_rule_backward(q, k, v, g, beta, dout, groups)
+    for x, y in zip(chunked, serial):
+        close(x.cpu(), y.cpu(), rtol=2e-2, cos_min=0.9999)
 
 
 @cuda
