@@ -19,7 +19,8 @@
 // The statements these kernels implement, and their check against autograd through
 // the token recurrence, are ``gated_delta_rule_backward_chunked`` in the package's
 // reference ops. Chunk-local matrices pass between kernels through a workspace in
-// global memory (about 640 KB per chunk at D = 128).
+// global memory (about 770 KB per chunk at D = 128; S0 and dS1 are also kept
+// transposed, so every product reads them along rows).
 #include "common.h"
 #include "sm100.cuh"
 
@@ -50,6 +51,9 @@ __device__ __forceinline__ void mm(float* out, int os, const float* A, int ars, 
   for (int i = 0; i < TR; ++i)
 #pragma unroll
     for (int j = 0; j < TN; ++j) c[i][j] = 0.f;
+  // K is a multiple of 8 at every call: unrolling keeps eight iterations' loads in
+  // flight (the B operand of several products streams from global memory)
+#pragma unroll 8
   for (int k = 0; k < K; ++k) {
     float a[TR], b[TN];
 #pragma unroll
@@ -117,7 +121,7 @@ struct Ws {
   float *qn, *kn, *u, *w, *vn, *dvn, *dq, *dk;  // [nck][C][D]
   float *tinv, *m, *a, *kk;                     // [nck][C][C]
   float *G, *gam, *ek, *beta, *rq, *rk, *dG;    // [nck][C]
-  float *F, *H, *P, *S0, *dS1;                  // [nck][D][D]
+  float *F, *H, *P, *S0, *dS1, *S0t, *dS1t;     // [nck][D][D] (t: transposed copies)
 };
 
 struct Args {
@@ -287,38 +291,49 @@ template <int D>
 __global__ void __launch_bounds__(NT, 1) gdnb_scan(Args a) {
   constexpr int JW = Shapes<D>::JW;
   extern __shared__ float sm[];
-  float* X = sm;             // [D][JW]
-  float* Xn = X + D * JW;    // [D][JW]
+  constexpr int XS = JW + 1;  // padded row stride: column-wise reads are conflict-free
+  float* X = sm;              // [D][XS]
+  float* Xn = X + D * XS;     // [D][XS]
   const int jb = blockIdx.x, h = blockIdx.y, bi = blockIdx.z;
   const int64_t ck0 = ((int64_t)bi * a.nv + h) * a.n;
   const int c0 = jb * JW;
   constexpr int STR = 4;                     // rows per thread
   constexpr int STN = (D * JW) / NT / STR;   // columns per thread (4 at D = 128, 1 at D = 64)
-  for (int i = threadIdx.x; i < D * JW; i += NT) X[i] = 0.f;
+  for (int i = threadIdx.x; i < D * XS; i += NT) X[i] = 0.f;
   __syncthreads();
   for (int c = 0; c < a.n; ++c) {
     float* S0 = a.w.S0 + (ck0 + c) * D * D;
-    for (int i = threadIdx.x; i < D * JW; i += NT) S0[(i / JW) * D + c0 + i % JW] = X[i];
+    float* S0t = a.w.S0t + (ck0 + c) * D * D;
+    for (int i = threadIdx.x; i < D * JW; i += NT) {
+      S0[(i / JW) * D + c0 + i % JW] = X[(i / JW) * XS + i % JW];
+      S0t[(c0 + i / D) * D + i % D] = X[(i % D) * XS + i / D];
+    }
     if (c + 1 < a.n) {
       const float* F = a.w.F + (ck0 + c) * D * D;
       const float* H = a.w.H + (ck0 + c) * D * D;
-      mm<D, JW, STR, STN>(Xn, JW, F, D, 1, X, JW, 1, D, 1.f, false);
+      mm<D, JW, STR, STN>(Xn, XS, F, D, 1, X, XS, 1, D, 1.f, false);
       __syncthreads();
-      for (int i = threadIdx.x; i < D * JW; i += NT) X[i] = Xn[i] + H[(i / JW) * D + c0 + i % JW];
+      for (int i = threadIdx.x; i < D * JW; i += NT)
+        X[(i / JW) * XS + i % JW] = Xn[(i / JW) * XS + i % JW] + H[(i / JW) * D + c0 + i % JW];
       __syncthreads();
     }
   }
-  for (int i = threadIdx.x; i < D * JW; i += NT) X[i] = 0.f;
+  for (int i = threadIdx.x; i < D * XS; i += NT) X[i] = 0.f;
   __syncthreads();
   for (int c = a.n - 1; c >= 0; --c) {
     float* dS1 = a.w.dS1 + (ck0 + c) * D * D;
-    for (int i = threadIdx.x; i < D * JW; i += NT) dS1[(i / JW) * D + c0 + i % JW] = X[i];
+    float* dS1t = a.w.dS1t + (ck0 + c) * D * D;
+    for (int i = threadIdx.x; i < D * JW; i += NT) {
+      dS1[(i / JW) * D + c0 + i % JW] = X[(i / JW) * XS + i % JW];
+      dS1t[(c0 + i / D) * D + i % D] = X[(i % D) * XS + i / D];
+    }
     if (c > 0) {
       const float* F = a.w.F + (ck0 + c) * D * D;
       const float* P = a.w.P + (ck0 + c) * D * D;
-      mm<D, JW, STR, STN>(Xn, JW, F, 1, D, X, JW, 1, D, 1.f, false);  // F^T X
+      mm<D, JW, STR, STN>(Xn, XS, F, 1, D, X, XS, 1, D, 1.f, false);  // F^T X
       __syncthreads();
-      for (int i = threadIdx.x; i < D * JW; i += NT) X[i] = Xn[i] + P[(i / JW) * D + c0 + i % JW];
+      for (int i = threadIdx.x; i < D * JW; i += NT)
+        X[(i / JW) * XS + i % JW] = Xn[(i / JW) * XS + i % JW] + P[(i / JW) * D + c0 + i % JW];
       __syncthreads();
     }
   }
@@ -347,6 +362,8 @@ __global__ void __launch_bounds__(NT, 1) gdnb_grad1(Args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* S0 = a.w.S0 + ck * D * D;
   const float* dS1 = a.w.dS1 + ck * D * D;
+  const float* S0t = a.w.S0t + ck * D * D;
+  const float* dS1t = a.w.dS1t + ck * D * D;
   const float* gam = a.w.gam + ck * C;
   const float* ek = a.w.ek + ck * C;
   for (int i = threadIdx.x; i < C * D; i += NT) {
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(NT, 1) gdnb_grad1(Args a) {
   mm_cd<D>(sDVN, PD, sA, 1, PC, sO, PD, 1, C, 1.f, false);   // A^T dO
   __syncthreads();
   mm_cd<D>(sDVN, PD, sKh, PD, 1, dS1, D, 1, D, 1.f, true);   // + Kh dS1
-  mm_cd<D>(sX, PD, sO, PD, 1, S0, 1, D, D, 1.f, false);      // dQg = dO S0^T
+  mm_cd<D>(sX, PD, sO, PD, 1, S0t, D, 1, D, 1.f, false);     // dQg = dO S0^T
   __syncthreads();
   store_cd<D>(a.w.vn + ck * C * D, sVN);
   store_cd<D>(a.w.dvn + ck * C * D, sDVN);
@@ -380,7 +397,7 @@ __global__ void __launch_bounds__(NT, 1) gdnb_grad1(Args a) {
     if (lane == 0) dG[r] += gam[r] * dot;
   }
   __syncthreads();
-  mm_cd<D>(sX, PD, sVN, PD, 1, dS1, 1, D, D, 1.f, false);    // dKh = VN dS1^T
+  mm_cd<D>(sX, PD, sVN, PD, 1, dS1t, D, 1, D, 1.f, false);   // dKh = VN dS1^T
   __syncthreads();
   float tsum = 0.f;  // per warp: sum over its rows of ek k.dKh
   for (int r = warp; r < C; r += NT / 32) {
@@ -488,7 +505,7 @@ __global__ void __launch_bounds__(NT, 1) gdnb_grad2b(Args a) {
   const int t0 = c * C;
   const int cnt = min(C, a.s - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* S0 = a.w.S0 + ck * D * D;
+  const float* S0t = a.w.S0t + ck * D * D;
   load_cd<D>(s1, a.w.dvn + ck * C * D);
   load_cc(sT, a.w.tinv + ck * C * C);
   if (threadIdx.x < C) {
@@ -500,7 +517,7 @@ __global__ void __launch_bounds__(NT, 1) gdnb_grad2b(Args a) {
     sdB[t] = 0.f;
   }
   __syncthreads();
-  mm_cd<D>(s2, PD, s1, PD, 1, S0, 1, D, D, -1.f, false);  // dW = -dVN S0^T
+  mm_cd<D>(s2, PD, s1, PD, 1, S0t, D, 1, D, -1.f, false);  // dW = -dVN S0^T
   __syncthreads();
   mm_cd<D>(sBk, PD, sT, 1, PC, s2, PD, 1, C, 1.f, false);  // dBk = T^-T dW
   mm_cd<D>(sBv, PD, sT, 1, PC, s1, PD, 1, C, 1.f, false);  // dBv = T^-T dVN
@@ -612,7 +629,7 @@ template <int D>
 static void run(Args a, int b) {
   constexpr int PD = D + 1;
   const int smem_setup = (5 * C * PD + 2 * C * PC + 4 * C) * 4;
-  const int smem_scan = 2 * D * Shapes<D>::JW * 4;
+  const int smem_scan = 2 * D * (Shapes<D>::JW + 1) * 4;
   const int smem_g1 = (6 * C * PD + C * PC + NT / 32 + C) * 4;
   const int smem_g2a = (4 * C * PD + 2 * C * PC + C) * 4;
   const int smem_g2b = (4 * C * PD + 2 * C * PC + 5 * C) * 4;
@@ -653,7 +670,7 @@ bool gdn_bwd_chunked(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at:
   auto cd = at::empty({8, nck * C * D}, f32);
   auto cc = at::empty({4, nck * C * C}, f32);
   auto cv = at::empty({7, nck * C}, f32);
-  auto dd = at::empty({5, nck * (int64_t)D * D}, f32);
+  auto dd = at::empty({7, nck * (int64_t)D * D}, f32);
   Args a{};
   a.q = reinterpret_cast<const bf16*>(q.data_ptr());
   a.k = reinterpret_cast<const bf16*>(k.data_ptr());
@@ -685,6 +702,7 @@ bool gdn_bwd_chunked(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at:
   p = dd.data_ptr<float>();
   const int64_t ndd = nck * (int64_t)D * D;
   a.w.F = p, a.w.H = p + ndd, a.w.P = p + 2 * ndd, a.w.S0 = p + 3 * ndd, a.w.dS1 = p + 4 * ndd;
+  a.w.S0t = p + 5 * ndd, a.w.dS1t = p + 6 * ndd;
   if (D == 64)
     run<64>(a, b);
   else

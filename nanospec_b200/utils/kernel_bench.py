@@ -173,8 +173,9 @@ def bench_gdn(a):
     # chunked form, chunk 64: per head about 4*S*64*d (intra-chunk) + 4*S*d*d (state) MACs forward
     flops = 2.0 * nv * (4 * s * 64 * d + 4 * s * d * d)
     kern = _kernel_times(lambda: vops.gated_delta_rule(q, k, v, g, beta, nv // nk))
+    bkern = _kernel_times(lambda: vops.gated_delta_rule_backward(q, k, v, g, beta, dout, nv // nk))
     return {"op": "gdn_chunk", "S": s, "heads": nv, "fwd_us": round(us, 1), "bwd_us": round(bus, 1),
-            "fwd_tflops": round(flops / us / 1e6, 2), "fwd_kernels_us": kern}
+            "fwd_tflops": round(flops / us / 1e6, 2), "fwd_kernels_us": kern, "bwd_kernels_us": bkern}
 
 
 def bench_verifier(a):
