@@ -158,7 +158,7 @@ __global__ void silu_mul_quant_kernel(const bf16* __restrict__ gu, int64_t T, in
     unpack8(*reinterpret_cast<const uint4*>(g + m), uv);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      h[i] = rb(rb(gv[i] / (1.f + expf(-gv[i]))) * uv[i]);
+      h[i] = rb(rb(__fdividef(gv[i], 1.f + __expf(-gv[i]))) * uv[i]);  // fast SiLU (bf16 result)
       am = fmaxf(am, fabsf(h[i]));
     }
   }
@@ -204,7 +204,7 @@ __global__ void gated_norm_quant_kernel(const bf16* __restrict__ x, const bf16* 
   float am = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float sg = zv[i] / (1.f + expf(-zv[i]));
+    const float sg = __fdividef(zv[i], 1.f + __expf(-zv[i]));  // fast SiLU
     y[i] = rb(rb(wv[i] * rb(xv[i] * inv)) * sg);
     am = fmaxf(am, fabsf(y[i]));
   }
@@ -223,9 +223,10 @@ __global__ void gated_norm_quant_kernel(const bf16* __restrict__ x, const bf16* 
 // once. Rows of a new sequence (t % s == 0) start with an empty window. K <= 4.
 constexpr int CONV_TOKENS = 16;
 
+template <int K>
 __global__ void __launch_bounds__(256) conv_silu_vec_kernel(const bf16* __restrict__ x, int64_t ld,
                                                             const bf16* __restrict__ w, bf16* __restrict__ y,
-                                                            int64_t rows, int s, int C, int K) {
+                                                            int64_t rows, int s, int C) {
   const int c8 = blockIdx.y * blockDim.x + threadIdx.x;
   if (c8 * 8 >= C) return;
   const int c = c8 * 8;
@@ -259,8 +260,10 @@ __global__ void __launch_bounds__(256) conv_silu_vec_kernel(const bf16* __restri
 #pragma unroll
       for (int e = 0; e < 8; ++e) win[j][e] = 0.f;
   }
-  for (int64_t r = r0; r < r1; ++r) {
-    if (r % s == 0 && r != r0) {
+  int pos = (int)(r0 % s);  // position of row r in its sequence (one division per thread)
+  for (int64_t r = r0; r < r1; ++r, ++pos) {
+    if (pos == s) {  // a new sequence starts: no history
+      pos = 0;
 #pragma unroll
       for (int j = 0; j < 3; ++j)
 #pragma unroll
@@ -273,12 +276,15 @@ __global__ void __launch_bounds__(256) conv_silu_vec_kernel(const bf16* __restri
     for (int e = 0; e < 8; ++e) {
       // taps j = 0..K-1 read rows t - (K-1) + j: the last K entries of [win0, win1, win2, cur]
       float acc = 0.f;
-      const float seq[4] = {win[0][e], win[1][e], win[2][e], cur[e]};
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (j < K) acc += wv[e][j] * seq[4 - K + j];
+      for (int j = 0; j < K; ++j) {
+        const int src = 4 - K + j;  // 0..2: window rows, 3: the current row
+        acc += wv[e][j] * (src == 3 ? cur[e] : win[src < 3 ? src : 0][e]);
+      }
+      // SiLU in fp32 with the fast exponential and division intrinsics; the bf16
+      // result differs from the accurate forms only in rare rounding ties
       const float zz = rb(acc);
-      o[e] = zz / (1.f + expf(-zz));
+      o[e] = __fdividef(zz, 1.f + __expf(-zz));
     }
     reinterpret_cast<uint4*>(y + r * C)[c8] = pack8(o);
 #pragma unroll
@@ -345,9 +351,15 @@ void conv_silu_vec(at::Tensor x, int64_t ld, at::Tensor w, at::Tensor y) {
   const int64_t rows = (int64_t)b * s;
   if (rows == 0) return;
   const dim3 grid((unsigned)((rows + vf::CONV_TOKENS - 1) / vf::CONV_TOKENS), (unsigned)((C / 8 + 255) / 256));
-  vf::conv_silu_vec_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), ld,
-                                                     reinterpret_cast<const bf16*>(w.data_ptr()),
-                                                     reinterpret_cast<bf16*>(y.data_ptr()), rows, s, C, K);
+  auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
+  auto* yp = reinterpret_cast<bf16*>(y.data_ptr());
+  switch (K) {
+    case 1: vf::conv_silu_vec_kernel<1><<<grid, 256, 0, stream()>>>(xp, ld, wp, yp, rows, s, C); break;
+    case 2: vf::conv_silu_vec_kernel<2><<<grid, 256, 0, stream()>>>(xp, ld, wp, yp, rows, s, C); break;
+    case 3: vf::conv_silu_vec_kernel<3><<<grid, 256, 0, stream()>>>(xp, ld, wp, yp, rows, s, C); break;
+    default: vf::conv_silu_vec_kernel<4><<<grid, 256, 0, stream()>>>(xp, ld, wp, yp, rows, s, C); break;
+  }
   NS_CUDA(cudaGetLastError());
 }
 

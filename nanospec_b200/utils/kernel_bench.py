@@ -178,6 +178,19 @@ def bench_gdn(a):
             "fwd_tflops": round(flops / us / 1e6, 2), "fwd_kernels_us": kern, "bwd_kernels_us": bkern}
 
 
+def bench_conv(a):
+    """Causal depthwise conv + SiLU over the q/k/v channels of the fused GDN
+    projection output (strided token rows), the verifier's shape by default."""
+    from nanospec_b200.ops import verifier_ops as vops
+    ld, ch = a.k, a.nout  # row stride of the projection output, conv channels
+    x = torch.randn(1, a.S, ld, device="cuda").bfloat16()
+    w = (torch.randn(ch, 4, device="cuda") * 0.3).bfloat16()
+    us = _time(lambda: vops.causal_conv_silu_rows(x, ld, w, ch), a.reps, a.warmup)
+    moved = a.S * ch * 2 * 2  # read and write the conv channels once
+    return {"op": "conv_silu", "S": a.S, "channels": ch, "us": round(us, 1),
+            "GBps": round(moved / us / 1e3, 1), "of_measured_hbm": _of_peak(moved / us / 1e3)}
+
+
 def bench_verifier(a):
     from nanospec_b200.models.verifier import (QwenStage, qwen3_5_27b_text_config, random_verifier_weights,
                                                stage_forward, synthetic_hf_config)
@@ -364,7 +377,7 @@ def bench_fused(a):
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("op", choices=("gemm", "adamw", "head", "attention", "fp8", "gdn", "gemm-suite",
-                                     "verifier", "fused"))
+                                     "verifier", "fused", "conv"))
     p.add_argument("--kind", choices=("fwd", "dgrad", "wgrad"), default="fwd")
     p.add_argument("--T", type=int, default=56)
     p.add_argument("--nout", type=int, default=5120)
@@ -383,7 +396,7 @@ def main(argv=None):
     a = p.parse_args(argv)
     fn = {"gemm": bench_gemm, "adamw": bench_adamw, "head": bench_head, "attention": bench_attention,
           "fp8": bench_fp8, "gdn": bench_gdn, "gemm-suite": bench_gemm_suite,
-          "verifier": bench_verifier, "fused": bench_fused}[a.op]
+          "verifier": bench_verifier, "fused": bench_fused, "conv": bench_conv}[a.op]
     print(json.dumps(fn(a)), flush=True)
 
 
