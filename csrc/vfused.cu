@@ -49,13 +49,26 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
-// Division as in the reference (v / s), kept exact: the reciprocal would round differently.
+// v / den rounded to nearest, as the reference's division, from r = RN(1 / den) and
+// one FMA correction. Markstein's theorem (Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
+// when r is the correctly rounded reciprocal and q0 is within one ulp of v / den,
+// q0 + (v - q0 den) r evaluated as a single FMA is the correctly rounded quotient.
+// The residual v - q0 den is exact by FMA. The theorem holds in the normal range,
+// which den >= FLT_MIN and |v / den| <= 448 give. Smaller quotients are far below
+// the least e4m3 subnormal and quantise to the same code either way.
+__device__ __forceinline__ float div_rn(float v, float den, float r) {
+  const float q0 = v * r;
+  return fmaf(fmaf(-q0, den, v), r, q0);
+}
+
 __device__ __forceinline__ uint32_t e4m3x4_div(float a, float b, float c, float d, float den) {
   const float v[4] = {a, b, c, d};
+  const float r = 1.f / den;
   uint32_t p = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float y = fminf(fmaxf(v[i] / den, -448.f), 448.f);
+    const float y = fminf(fmaxf(div_rn(v[i], den, r), -448.f), 448.f);
     p |= (uint32_t)__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3) << (8 * i);
   }
   return p;
