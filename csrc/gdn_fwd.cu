@@ -32,7 +32,7 @@ using bf16 = __nv_bfloat16;
 namespace gdn {
 
 constexpr int C = 64;       // chunk length
-constexpr int CP = C + 4;   // padded row length of [D][C] tiles in shared memory
+constexpr int CP = C + 1;   // row length of the [D][C] transpose buffer: lanes 4 rows apart land 4 banks apart
 constexpr int NT = 256;     // threads per CTA (both kernels)
 
 __device__ __forceinline__ float bf(bf16 x) { return __bfloat162float(x); }
@@ -369,7 +369,8 @@ __global__ void __launch_bounds__(NT, 2) gdn_prep_kernel(const bf16* __restrict_
       float* ut = Uo + ck * D * C;
       for (int idx = tid; idx < D * C / 4; idx += NT) {
         const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
-        *reinterpret_cast<float4*>(&ut[e * C + i4]) = *reinterpret_cast<const float4*>(&tr[e * CP + i4]);
+        const float* src = &tr[e * CP + i4];
+        *reinterpret_cast<float4*>(&ut[e * C + i4]) = make_float4(src[0], src[1], src[2], src[3]);
       }
     } else {
       const int slice = e0 / dvs, el = e0 % dvs;
@@ -385,7 +386,8 @@ __global__ void __launch_bounds__(NT, 2) gdn_prep_kernel(const bf16* __restrict_
       float* wt = reinterpret_cast<float*>(Wo) + ck * D * C;
       for (int idx = tid; idx < D * C / 4; idx += NT) {
         const int e = idx / (C / 4), i4 = (idx % (C / 4)) * 4;
-        *reinterpret_cast<float4*>(&wt[e * C + i4]) = *reinterpret_cast<const float4*>(&tr[e * CP + i4]);
+        const float* src = &tr[e * CP + i4];
+        *reinterpret_cast<float4*>(&wt[e * C + i4]) = make_float4(src[0], src[1], src[2], src[3]);
       }
     }
   }
