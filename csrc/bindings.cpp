@@ -62,6 +62,9 @@ void ag_gemm(int64_t id, int64_t src_off, int64_t ss, at::Tensor resident, int64
              at::Tensor x, at::Tensor out, at::Tensor flags, at::Tensor claim, int64_t epoch, int64_t poll_limit);
 void gemm_rs(int64_t id, int64_t slot_off, int64_t ss, int64_t g_off, at::Tensor dy, at::Tensor x);
 void peer_push(int64_t id, int64_t slot_off, int64_t ss, at::Tensor src, int64_t lo, int64_t hi);
+void peer_put(int64_t id, int64_t dst, int64_t dst_off, at::Tensor src);
+void peer_signal_to(int64_t id, int64_t flags_off, int64_t channel, int64_t dst, int64_t seq);
+void peer_wait_from(int64_t id, int64_t flags_off, int64_t channel, int64_t src, int64_t seq, int64_t poll_limit);
 void peer_signal(int64_t id, int64_t flags_off, int64_t channel, int64_t seq);
 void peer_wait(int64_t id, int64_t flags_off, int64_t channel, int64_t seq, int64_t poll_limit);
 std::vector<at::Tensor> gdn_chunk_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
@@ -131,6 +134,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ag_gemm", &ns::ag_gemm);
   m.def("gemm_rs", &ns::gemm_rs);
   m.def("peer_push", &ns::peer_push);
+  m.def("peer_put", &ns::peer_put);
+  m.def("peer_signal_to", &ns::peer_signal_to);
+  m.def("peer_wait_from", &ns::peer_wait_from);
   m.def("peer_signal", &ns::peer_signal);
   m.def("peer_wait", &ns::peer_wait);
   m.def("gdn_chunk_bwd", &ns::gdn_chunk_bwd);

@@ -176,6 +176,46 @@ __global__ void peer_reduce_avg_scalar_kernel(PeerTable t, int world, int rank, 
   }
 }
 
+// ---------------------------------------------------------------------------- one-to-one
+// dst window of rank `dst` at byte dst_off <- this rank's src (n16 16-byte chunks).
+__global__ void peer_put_kernel(PeerTable t, int dst, int64_t dst_off, const uint4* __restrict__ src, int64_t n16) {
+  uint64_t base = t.base[0];
+#pragma unroll
+  for (int i = 1; i < MAX_PEERS; ++i) base = dst == i ? t.base[i] : base;
+  uint4* out = reinterpret_cast<uint4*>(base + dst_off);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = src[i];
+  __threadfence_system();  // the stores reach `dst` before a later signal
+}
+
+// flags_dst[channel][rank] = seq (one destination).
+__global__ void peer_signal_to_kernel(PeerTable t, int64_t flags_off, int channel, int rank, int dst, unsigned seq) {
+  if (threadIdx.x != 0) return;
+  uint64_t base = t.base[0];
+#pragma unroll
+  for (int i = 1; i < MAX_PEERS; ++i) base = dst == i ? t.base[i] : base;
+  __threadfence_system();
+  st_release_sys(reinterpret_cast<unsigned*>(base + flags_off) + channel * MAX_PEERS + rank, seq);
+}
+
+// wait until flags_self[channel][src] >= seq (bounded).
+__global__ void peer_wait_from_kernel(PeerTable t, int64_t flags_off, int channel, int rank, int src, unsigned seq,
+                                      int* err, long long limit) {
+  if (threadIdx.x != 0) return;
+  uint64_t base = t.base[0];
+#pragma unroll
+  for (int i = 1; i < MAX_PEERS; ++i) base = rank == i ? t.base[i] : base;
+  const unsigned* f = reinterpret_cast<const unsigned*>(base + flags_off) + channel * MAX_PEERS + src;
+  long long i = 0;
+  while ((int)(ld_acquire_sys(f) - seq) < 0) {
+    if (++i > limit) {
+      atomicExch(err, 2);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
 // ============================================================================ host
 struct Window {
   void* ptr = nullptr;
@@ -341,6 +381,37 @@ void peer_reduce_local(int64_t id, int64_t slot_off, int64_t ss_elems, at::Tenso
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((ss_elems / 8 + 255) / 256, (int64_t)num_sms() * 2));
   local_reduce_avg_kernel<<<blocks, 256, 0, stream()>>>(slot + (int64_t)w->rank * ss_elems, slot, w->world, w->rank,
                                                         ss_elems, reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
+  NS_CUDA(cudaGetLastError());
+}
+
+// Copies `src` (16-byte aligned, a multiple of 16 bytes) into rank `dst`'s window at
+// byte `dst_off`, by SM stores over NVLink.
+void peer_put(int64_t id, int64_t dst, int64_t dst_off, at::Tensor src) {
+  Window* w = g_windows.at(id);
+  const int64_t bytes = src.numel() * src.element_size();
+  NS_CHECK(src.is_contiguous() && bytes % 16 == 0 && reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0 &&
+               dst_off % 16 == 0,
+           "peer_put: 16-byte aligned contiguous source and destination expected");
+  NS_CHECK(dst >= 0 && dst < w->world, "peer_put: destination rank outside the window's world");
+  if (bytes == 0) return;
+  peer_put_kernel<<<blocks_for(bytes / 16), 256, 0, stream()>>>(w->table, (int)dst, dst_off,
+                                                                reinterpret_cast<const uint4*>(src.data_ptr()),
+                                                                bytes / 16);
+  NS_CUDA(cudaGetLastError());
+}
+
+void peer_signal_to(int64_t id, int64_t flags_off, int64_t channel, int64_t dst, int64_t seq) {
+  Window* w = g_windows.at(id);
+  NS_CHECK(dst >= 0 && dst < w->world, "peer_signal_to: destination rank outside the window's world");
+  peer_signal_to_kernel<<<1, 32, 0, stream()>>>(w->table, flags_off, (int)channel, w->rank, (int)dst, (unsigned)seq);
+  NS_CUDA(cudaGetLastError());
+}
+
+void peer_wait_from(int64_t id, int64_t flags_off, int64_t channel, int64_t src, int64_t seq, int64_t poll_limit) {
+  Window* w = g_windows.at(id);
+  NS_CHECK(src >= 0 && src < w->world, "peer_wait_from: source rank outside the window's world");
+  peer_wait_from_kernel<<<1, 32, 0, stream()>>>(w->table, flags_off, (int)channel, w->rank, (int)src, (unsigned)seq,
+                                               device_error_flag(), (long long)poll_limit);
   NS_CUDA(cudaGetLastError());
 }
 

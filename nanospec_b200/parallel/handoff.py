@@ -19,13 +19,22 @@ Here:
   from ``last_hidden`` vocabulary-chunk by chunk, so the [N, S, V] tensor never exists;
 * with a colocated topology (verifier partitions on the training GPUs), rows that a
   rank both produces and trains on are handed over without any transfer;
-* hand-off messages use their own process group (its own NCCL communicator), and
-  every trainer posts its receives before any verifier compute starts. Pipeline and
-  hand-off messages therefore can neither be matched against each other (they have
-  identical shapes) nor wait on each other.
+* on CUDA the hand-off is by peer stores (``HandoffWindow``): every training rank
+  exposes receive slots (one per capture layer and one for the final hidden state)
+  in a CUDA-IPC window, the verifier rank that produces trainer r's row stores it
+  straight into r's slot over NVLink and raises a per-slot flag, and trainer r
+  waits on those flags (bounded) and trains on the slots in place. Trainer r
+  releases its slots at the start of the next step (a flag the producers wait on
+  before storing again). ``NANOSPEC_HANDOFF=nccl`` keeps the point-to-point sends;
+* NCCL hand-off messages use their own process group (its own NCCL communicator),
+  and every trainer posts its receives before any verifier compute starts. Pipeline
+  and hand-off messages therefore can neither be matched against each other (they
+  have identical shapes) nor wait on each other.
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -100,6 +109,71 @@ class Teacher(nn.Module):
         return next(r for r, (a, b) in self.partitions.items() if a <= layer < b)
 
 
+class HandoffWindow:
+    """Receive slots of every training rank in peer memory, and the flags around them.
+
+    Collective over the node (all ranks create it together). Slot i of trainer r
+    holds row r of capture i (i < len(capture)) or of the final normed hidden state
+    (i = len(capture)), [s, width] bf16. Flags (``[channel][source rank]`` words in
+    the receiver's window): channel DATA + i, set by the producer of slot i with the
+    step's sequence number; channel FREE, set by a trainer on each producer once the
+    previous step's slots may be overwritten.
+    """
+
+    FLAGS = 4096
+    DATA, FREE = 16, 64
+
+    def __init__(self, group, training, nslots, s, width):
+        from ..ops._ext import cuda_ops
+        self.C = cuda_ops()
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.s, self.width, self.nslots = s, width, nslots
+        self.slot_bytes = (s * width * 2 + 255) // 256 * 256
+        size = self.FLAGS + (nslots * self.slot_bytes if training else 0)
+        self.id, _ = self.C.window_create(size, self.rank, self.world)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.C.window_ipc_handle(self.id).tolist(), group=group)
+        self.C.window_open(self.id, torch.tensor(handles, dtype=torch.uint8))
+        self.seq = 0
+        t = float(os.environ.get("NANOSPEC_PEER_TIMEOUT_S", 60))
+        self.poll_limit = int(t / 200e-9)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    def offset(self, slot):
+        return self.FLAGS + slot * self.slot_bytes
+
+    def view(self, slot):
+        return self.C.window_view(self.id, self.offset(slot), self.s * self.width,
+                                  torch.bfloat16).view(1, self.s, self.width)
+
+    def put(self, dst, slot, row):
+        self.C.peer_put(self.id, dst, self.offset(slot), row.contiguous())
+        self.C.peer_signal_to(self.id, 0, self.DATA + slot, dst, self.seq)
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.C.window_close(self.id)
+
+
+def _handoff_window(verifier, s, width):
+    """The Teacher's hand-off window for sequence length ``s`` (re-created collectively
+    when ``s`` changes), or None when the NCCL hand-off is in use."""
+    node = verifier.node
+    if (verifier.handoff_group is None or node.device.type != "cuda"
+            or os.environ.get("NANOSPEC_HANDOFF", "peer") == "nccl"):
+        return None
+    win = getattr(verifier, "_handoff_window", None)
+    if win is None or win.s != s or win.width != width:
+        if win is not None:
+            win.close()
+        win = HandoffWindow(verifier.handoff_group, node.training, len(verifier.capture) + 1, s, width)
+        verifier._handoff_window = win
+    return win
+
+
 @torch.no_grad()
 def run_verifier(ids, verifier: Teacher, microbatch_rows: int = 1):
     """Runs the verifier on the full [N, S] batch; returns (TeacherBatch | None, ids row).
@@ -121,6 +195,9 @@ def run_verifier(ids, verifier: Teacher, microbatch_rows: int = 1):
     ntrain = node.train_gpus
     caps = verifier.capture
     hg = verifier.handoff_group
+    win = _handoff_window(verifier, s, width)
+    if win is not None:
+        return _run_verifier_peer(ids, verifier, win, microbatch_rows)
     # Receive buffers of this trainer, posted before any compute so sends never block.
     recv_feats = {}
     recv_last = None
@@ -180,4 +257,71 @@ def run_verifier(ids, verifier: Teacher, microbatch_rows: int = 1):
         feats = [local_feats.get(layer, recv_feats[layer]) for layer in caps]
         last = local_last if local_last is not None else recv_last
         return TeacherBatch(feats, last, None), ids[node.rank:node.rank + 1]
+    return None, ids
+
+
+def _run_verifier_peer(ids, verifier, win, microbatch_rows):
+    """``run_verifier`` with the hand-off by peer stores into ``win`` (see module doc)."""
+    node, stage = verifier.node, verifier.stage
+    ranks = node.inference_ranks
+    b, s = ids.shape
+    width = verifier.config["hidden_size"]
+    ntrain = node.train_gpus
+    caps = verifier.capture
+    last_slot = len(caps)
+    C = win.C
+    win.seq += 1
+    seq = win.seq
+
+    def owner(slot):
+        return verifier.owner(caps[slot]) if slot < last_slot else ranks[-1]
+
+    # This trainer's slots of the previous step are no longer read (its kernels are
+    # ordered before this signal on the stream): their producers may store again.
+    if node.training and seq > 1:
+        for p in sorted({owner(i) for i in range(last_slot + 1)} - {node.rank}):
+            C.peer_signal_to(win.id, 0, win.FREE, p, seq - 1)
+    local = {}
+    if stage is not None:
+        idx = ranks.index(node.rank)
+        last_stage = idx == len(ranks) - 1
+        released = set()  # trainers whose previous-step slots this rank may overwrite
+        pending = []
+        for r0 in range(0, b, microbatch_rows):
+            r1 = min(b, r0 + microbatch_rows)
+            if stage.embed_tokens is not None:
+                x = ids[r0:r1]
+            else:
+                x = torch.empty(r1 - r0, s, width, device=node.device, dtype=torch.bfloat16)
+                dist.recv(x, src=ranks[idx - 1])
+            out, captured = stage_forward(stage, x, capture=caps)
+            rows_of = [(i, captured[caps[i]]) for i in range(last_slot) if caps[i] in captured]
+            if last_stage:
+                rows_of.append((last_slot, out))
+            for i, h in rows_of:
+                for row in range(r0, min(r1, ntrain)):
+                    piece = h[row - r0:row - r0 + 1]
+                    if row == node.rank:
+                        local[i] = piece
+                        continue
+                    if seq > 1 and row not in released:
+                        # wait (on the device, after this step's compute was queued, so
+                        # the verifier overlaps the trainer's previous step) until
+                        # trainer `row` released the slots of the previous step
+                        C.peer_wait_from(win.id, 0, win.FREE, row, seq - 1, win.poll_limit)
+                        released.add(row)
+                    win.put(row, i, piece)
+            if not last_stage:
+                pending.append(dist.isend(out.contiguous(), ranks[idx + 1]))
+        for w in pending:
+            w.wait()
+    if node.training:
+        got = []
+        for i in range(last_slot + 1):
+            if i in local:
+                got.append(local[i])
+            else:
+                C.peer_wait_from(win.id, 0, win.DATA + i, owner(i), seq, win.poll_limit)
+                got.append(win.view(i))
+        return TeacherBatch(got[:last_slot], got[last_slot], None), ids[node.rank:node.rank + 1]
     return None, ids

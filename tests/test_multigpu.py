@@ -297,3 +297,40 @@ def test_fused_schedules_bitwise_and_match_nccl():
 @pytest.mark.skipif(ngpu < 4, reason="needs 4 GPUs")
 def test_fused_kernels_four_ranks():
     run_ranks(4, _fused_kernels)
+
+
+def _handoff(rank, world, ckpt_path, train_gpus):
+    """Peer-store hand-off of the split layout over three steps (the slot release and
+    reuse protocol): every trainer row equals the whole verifier run on that GPU."""
+    from nanospec_b200.config import Topology
+    from nanospec_b200.models.verifier import Checkpoint, QwenStage, stage_forward
+    from nanospec_b200.ops._ext import cuda_ops
+    from nanospec_b200.parallel.handoff import Teacher
+    node = N.Node(train_gpus, topology=Topology(world=world, train_gpus=train_gpus))
+    capture = (1, 3)
+    teacher = Teacher(node, ckpt_path, capture)
+    full = QwenStage(Checkpoint(ckpt_path), 0, 4, device=node.device, first=True, last=True) if node.training else None
+    for step in range(3):
+        ids = torch.randint(0, 512, (train_gpus, 40), generator=torch.Generator().manual_seed(3 + step)).to(node.device)
+        res = N.train(ids, verifier=teacher)
+        assert getattr(teacher, "_handoff_window", None) is not None, "peer hand-off not in use"
+        if node.training:
+            x, cap = stage_forward(full, ids[rank:rank + 1], capture=capture)
+            tb = res.teacher
+            for got, layer in zip(tb.hidden_states, capture):
+                assert torch.equal(got, cap[layer]), (step, layer)
+            assert torch.equal(tb.last_hidden, x), step
+        torch.cuda.synchronize()
+    assert cuda_ops().device_error() == 0
+    teacher._handoff_window.close()
+
+
+@two_gpus
+@pytest.mark.parametrize("train_gpus", [1, 2])
+def test_verifier_handoff_by_peer_stores(train_gpus):
+    from nanospec_b200.models.verifier import tiny_hybrid_text_config, write_synthetic_checkpoint
+    with tempfile.TemporaryDirectory() as d:
+        cfg = tiny_hybrid_text_config()
+        cfg["head_dim"] = 32  # the tcgen05 verifier attention takes head dims 32..256
+        path = write_synthetic_checkpoint(os.path.join(d, "ck"), cfg, fp8=False, seed=2)
+        run_ranks(2, _handoff, str(path), train_gpus)
