@@ -75,6 +75,10 @@ void fp8_gemm(at::Tensor q, at::Tensor sa, at::Tensor w, at::Tensor scale_inv, a
 void quant_e4m3(at::Tensor x, at::Tensor q, at::Tensor s);
 void add_norm(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps, c10::optional<at::Tensor> x_out,
               c10::optional<at::Tensor> n_out, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> s_out);
+void add_norm_peer(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps,
+                   c10::optional<at::Tensor> x_out, c10::optional<at::Tensor> n_out, c10::optional<at::Tensor> q_out,
+                   c10::optional<at::Tensor> s_out, int64_t win, int64_t x_dst, int64_t x_off, int64_t n_dst,
+                   int64_t n_off);
 void silu_mul_quant(at::Tensor gu, at::Tensor q, at::Tensor s);
 void gated_norm_quant(at::Tensor x, at::Tensor z, int64_t nv, int64_t z_ts, at::Tensor w, double eps, at::Tensor q,
                       at::Tensor s);
@@ -144,6 +148,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_e4m3", &ns::quant_e4m3);
   m.def("add_norm", &ns::add_norm, py::arg("x"), py::arg("y"), py::arg("w"), py::arg("eps"), py::arg("x_out"),
         py::arg("n_out"), py::arg("q_out"), py::arg("s_out"));
+  m.def("add_norm_peer", &ns::add_norm_peer);
   m.def("silu_mul_quant", &ns::silu_mul_quant);
   m.def("gated_norm_quant", &ns::gated_norm_quant);
   m.def("conv_silu_vec", &ns::conv_silu_vec);

@@ -19,6 +19,7 @@
 // Quantisation follows the reference statement on the bf16 value v:
 // s = amax / 448, q = e4m3(clamp(v / max(s, FLT_MIN), -448, 448)) (saturating).
 #include "common.h"
+#include "peer.h"
 #include "sm100.cuh"
 
 #include <cuda_fp8.h>
@@ -80,7 +81,8 @@ constexpr int AN_MAX_CPT = 4;  // chunks of 8 per thread: rows up to 8192 channe
 __global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ y,
                                                               const bf16* __restrict__ w, float eps, int H,
                                                               bf16* __restrict__ x_out, bf16* __restrict__ n_out,
-                                                              uint8_t* __restrict__ q_out, float* __restrict__ s_out) {
+                                                              uint8_t* __restrict__ q_out, float* __restrict__ s_out,
+                                                              bf16* __restrict__ x_peer, bf16* __restrict__ n_peer) {
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
   const int nch = H / 8;
@@ -96,7 +98,9 @@ __global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __rest
         unpack8(reinterpret_cast<const uint4*>(y + row * H)[c], t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[j][i] = rb(v[j][i] + t[i]);
-        reinterpret_cast<uint4*>(x_out + row * H)[c] = pack8(v[j]);
+        const uint4 pk = pack8(v[j]);
+        reinterpret_cast<uint4*>(x_out + row * H)[c] = pk;
+        if (x_peer) reinterpret_cast<uint4*>(x_peer + row * H)[c] = pk;  // hand-off store to a trainer
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
@@ -129,6 +133,7 @@ __global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __rest
 #pragma unroll
       for (int i = 0; i < 8; ++i) nv[i] = rb(v[j][i] * inv * (1.f + wv[i]));
       if (n_out) reinterpret_cast<uint4*>(n_out + row * H)[c] = pack8(nv);
+      if (n_peer) reinterpret_cast<uint4*>(n_peer + row * H)[c] = pack8(nv);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) nv[i] = 0.f;
@@ -150,6 +155,7 @@ __global__ void __launch_bounds__(AN_THREADS) add_norm_kernel(const bf16* __rest
       }
     }
   }
+  if (x_peer || n_peer) __threadfence_system();  // peer stores land before a later flag
 }
 
 // gu [T, 2m] = [gate | up]; h = bf16(bf16(silu(gate)) * up) -> e4m3 + scales [T, m/128].
@@ -325,7 +331,44 @@ void add_norm(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double ep
   vf::add_norm_kernel<<<(unsigned)rows, vf::AN_THREADS, 0, stream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(p(y)),
       reinterpret_cast<const bf16*>(w.data_ptr()), (float)eps, H, reinterpret_cast<bf16*>(p(x_out)),
-      reinterpret_cast<bf16*>(p(n_out)), reinterpret_cast<uint8_t*>(p(q_out)), reinterpret_cast<float*>(p(s_out)));
+      reinterpret_cast<bf16*>(p(n_out)), reinterpret_cast<uint8_t*>(p(q_out)), reinterpret_cast<float*>(p(s_out)),
+      nullptr, nullptr);
+  NS_CUDA(cudaGetLastError());
+}
+
+// add_norm whose epilogue also stores x_out (x_dst >= 0) and / or n_out (n_dst >= 0)
+// into rank x_dst's / n_dst's window of `win` at byte x_off / n_off, same row layout:
+// the verifier -> trainer hand-off written by the producing kernel.
+void add_norm_peer(at::Tensor x, c10::optional<at::Tensor> y, at::Tensor w, double eps,
+                   c10::optional<at::Tensor> x_out, c10::optional<at::Tensor> n_out, c10::optional<at::Tensor> q_out,
+                   c10::optional<at::Tensor> s_out, int64_t win, int64_t x_dst, int64_t x_off, int64_t n_dst,
+                   int64_t n_off) {
+  check_bf16(x, "x");
+  const int H = (int)x.size(-1);
+  const int64_t rows = x.numel() / H;
+  NS_CHECK(x.is_contiguous() && H % 8 == 0 && H / 8 <= vf::AN_THREADS * vf::AN_MAX_CPT, "add_norm: row width");
+  NS_CHECK(!q_out || H % 128 == 0, "add_norm: quantised output needs 128-multiple rows");
+  NS_CHECK(!y || x_out, "add_norm: the residual sum needs x_out");
+  NS_CHECK(x_dst < 0 || (y && x_out), "add_norm_peer: the residual store needs y and x_out");
+  NS_CHECK(n_dst < 0 || n_out, "add_norm_peer: the normed store needs n_out");
+  NS_CHECK(x_off % 16 == 0 && n_off % 16 == 0, "add_norm_peer: 16-byte aligned destinations");
+  if (rows == 0) return;
+  const WindowInfo wi = window_info(win);
+  // Offsets come from the slot layout every rank shares (the caller's own window may
+  // be smaller than the destination's, so its size bounds nothing here).
+  auto peer = [&](int64_t dst, int64_t off) -> bf16* {
+    if (dst < 0) return nullptr;
+    NS_CHECK(dst < wi.world, "add_norm_peer: destination rank outside the window's world");
+    const uint64_t base = wi.table.base[dst];
+    NS_CHECK(base != 0, "add_norm_peer: destination window not open");
+    return reinterpret_cast<bf16*>(base + off);
+  };
+  auto p = [](const c10::optional<at::Tensor>& t) -> void* { return t ? t->data_ptr() : nullptr; };
+  vf::add_norm_kernel<<<(unsigned)rows, vf::AN_THREADS, 0, stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(p(y)),
+      reinterpret_cast<const bf16*>(w.data_ptr()), (float)eps, H, reinterpret_cast<bf16*>(p(x_out)),
+      reinterpret_cast<bf16*>(p(n_out)), reinterpret_cast<uint8_t*>(p(q_out)), reinterpret_cast<float*>(p(s_out)),
+      peer(x_dst, x_off), peer(n_dst, n_off));
   NS_CUDA(cudaGetLastError());
 }
 

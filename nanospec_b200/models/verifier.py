@@ -513,12 +513,26 @@ def _attention_fused(attn: QwenAttention, nq, b, s, device, dtype):
 
 
 @torch.no_grad()
-def _stage_forward_fused(stage: QwenStage, x, capture, on_capture):
+def _stage_forward_fused(stage: QwenStage, x, capture, on_capture, handoff=None):
     """CUDA forward with fused projections and fused producers: every residual add is
     fused with the following (1+w)-RMSNorm, and every FP8 projection input leaves its
     producer already quantised (e4m3 + 1 x 128 scales). Same math as the statement
-    path below; only roundings inside fp32 reductions differ."""
+    path below; only roundings inside fp32 reductions differ.
+
+    ``handoff``: ``{layer index or "final": (window id, rank, byte offset)}``; the
+    add+norm kernel that produces a captured residual (or the final normed hidden
+    state) also stores it into that rank's peer window, and the entry is removed
+    (entries left over were produced by other kernels: the caller copies them)."""
     b, s, h = x.shape
+    handoff = {} if handoff is None else handoff
+
+    def peer(li, final):
+        xt = handoff.pop(li) if li in capture and li in handoff else None
+        nt = handoff.pop("final") if final and "final" in handoff else None
+        if xt is None and nt is None:
+            return None
+        win = (xt or nt)[0]
+        return (win, None if xt is None else xt[1:], None if nt is None else nt[1:])
     layers = list(stage.layers)
     ln = layers[0].input_layernorm
     _, n_bf, nq = vops.add_norm(x, None, ln.weight, ln.eps, want_bf16=layers[0].linear_attn is not None,
@@ -540,9 +554,9 @@ def _stage_forward_fused(stage: QwenStage, x, capture, on_capture):
             nxt = layers[i + 1]
             ln = nxt.input_layernorm
             x, n_bf, nq = vops.add_norm(x, down, ln.weight, ln.eps, want_bf16=nxt.linear_attn is not None,
-                                        want_q=True)
+                                        want_q=True, peer=peer(li, False))
         elif stage.norm is not None:
-            x, final, _ = vops.add_norm(x, down, stage.norm.weight, stage.norm.eps)
+            x, final, _ = vops.add_norm(x, down, stage.norm.weight, stage.norm.eps, peer=peer(li, True))
         else:
             x = vops.add(x, down)
         if li in capture:
@@ -553,19 +567,20 @@ def _stage_forward_fused(stage: QwenStage, x, capture, on_capture):
 
 
 @torch.no_grad()
-def stage_forward(stage: QwenStage, x_or_ids, capture=(), on_capture=None):
+def stage_forward(stage: QwenStage, x_or_ids, capture=(), on_capture=None, handoff=None):
     """Run the stage's layers. Returns (output, {layer_index: hidden}).
 
     ``x_or_ids``: token ids [b, s] for the first stage, else the hidden state [b, s, H].
     ``on_capture(layer_index, hidden)``, when given, receives each captured decoder
     output as soon as it exists (used to start the trainer hand-off early).
+    ``handoff`` (fused CUDA path): see ``_stage_forward_fused``.
     """
     if stage.embed_tokens is not None:
         x = vops.embedding(x_or_ids, stage.embed_tokens.weight)
     else:
         x = x_or_ids
     if getattr(stage, "fused", False) and x.is_cuda and len(stage.layers) > 0:
-        return _stage_forward_fused(stage, x, capture, on_capture)
+        return _stage_forward_fused(stage, x, capture, on_capture, handoff)
     captured = {}
     for li, layer in enumerate(stage.layers, start=stage.start):
         n = vops.qwen_norm(x, layer.input_layernorm.weight, layer.input_layernorm.eps)

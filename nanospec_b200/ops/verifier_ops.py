@@ -193,17 +193,28 @@ def fp8_gemm(q, s, w, scale_inv):
     return out
 
 
-def add_norm(x, y, w, eps, *, want_bf16=True, want_q=False):
+def add_norm(x, y, w, eps, *, want_bf16=True, want_q=False, peer=None):
     """x' = x + y (y may be None), n = (1+w)-RMSNorm(x'); returns (x', n bf16 or None,
-    (codes, scales) or None). One kernel; the quantised form feeds ``fp8_gemm``."""
+    (codes, scales) or None). One kernel; the quantised form feeds ``fp8_gemm``.
+
+    ``peer``: ``(window id, (x_dst, x_off) or None, (n_dst, n_off) or None)``; the
+    kernel's epilogue then also stores x' / n into rank x_dst's / n_dst's peer window
+    at those byte offsets (the verifier -> trainer hand-off)."""
     h = x.shape[-1]
     rows = x.numel() // h
     x2 = x.reshape(rows, h)
     xo = torch.empty_like(x2) if y is not None else None
-    n = torch.empty_like(x2) if want_bf16 else None
+    n = torch.empty_like(x2) if (want_bf16 or (peer is not None and peer[2] is not None)) else None
     q = torch.empty(rows, h, device=x.device, dtype=torch.uint8) if want_q else None
     sc = torch.empty(rows, h // 128, device=x.device, dtype=torch.float32) if want_q else None
-    _c().add_norm(x2, None if y is None else y.reshape(rows, h), w, float(eps), xo, n, q, sc)
+    y2 = None if y is None else y.reshape(rows, h)
+    if peer is None:
+        _c().add_norm(x2, y2, w, float(eps), xo, n, q, sc)
+    else:
+        win, xt, nt = peer
+        xd, xof = xt if xt is not None else (-1, 0)
+        nd, nof = nt if nt is not None else (-1, 0)
+        _c().add_norm_peer(x2, y2, w, float(eps), xo, n, q, sc, int(win), int(xd), int(xof), int(nd), int(nof))
     xo = x if xo is None else xo.view(x.shape)
     return xo, (None if n is None else n.view(x.shape)), ((q, sc) if want_q else None)
 

@@ -114,10 +114,12 @@ class HandoffWindow:
 
     Collective over the node (all ranks create it together). Slot i of trainer r
     holds row r of capture i (i < len(capture)) or of the final normed hidden state
-    (i = len(capture)), [s, width] bf16. Flags (``[channel][source rank]`` words in
-    the receiver's window): channel DATA + i, set by the producer of slot i with the
-    step's sequence number; channel FREE, set by a trainer on each producer once the
-    previous step's slots may be overwritten.
+    (i = len(capture)), [s, width] bf16, in two sets used by alternate steps. Flags
+    (``[channel][source rank]`` words in the receiver's window): channel DATA + i, set
+    by the producer of slot i with the step's sequence number; channel FREE, set by a
+    trainer on each producer when a step's slot set is no longer read. A producer
+    writes step t's set after FREE reached t - 2, which the trainer raised at the
+    start of step t - 1, so the wait never holds the verifier back in steady state.
     """
 
     FLAGS = 4096
@@ -130,7 +132,7 @@ class HandoffWindow:
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.s, self.width, self.nslots = s, width, nslots
         self.slot_bytes = (s * width * 2 + 255) // 256 * 256
-        size = self.FLAGS + (nslots * self.slot_bytes if training else 0)
+        size = self.FLAGS + (2 * nslots * self.slot_bytes if training else 0)
         self.id, _ = self.C.window_create(size, self.rank, self.world)
         handles = [None] * self.world
         dist.all_gather_object(handles, self.C.window_ipc_handle(self.id).tolist(), group=group)
@@ -141,16 +143,18 @@ class HandoffWindow:
         torch.cuda.synchronize()
         dist.barrier(group=group)
 
-    def offset(self, slot):
-        return self.FLAGS + slot * self.slot_bytes
+    def offset(self, slot, seq):
+        return self.FLAGS + ((seq & 1) * self.nslots + slot) * self.slot_bytes
 
-    def view(self, slot):
-        return self.C.window_view(self.id, self.offset(slot), self.s * self.width,
+    def view(self, slot, seq):
+        return self.C.window_view(self.id, self.offset(slot, seq), self.s * self.width,
                                   torch.bfloat16).view(1, self.s, self.width)
 
-    def put(self, dst, slot, row):
-        self.C.peer_put(self.id, dst, self.offset(slot), row.contiguous())
-        self.C.peer_signal_to(self.id, 0, self.DATA + slot, dst, self.seq)
+    def put(self, dst, slot, row, seq):
+        self.C.peer_put(self.id, dst, self.offset(slot, seq), row.contiguous())
+
+    def signal(self, dst, slot, seq):
+        self.C.peer_signal_to(self.id, 0, self.DATA + slot, dst, seq)
 
     def close(self):
         torch.cuda.synchronize()
@@ -261,7 +265,12 @@ def run_verifier(ids, verifier: Teacher, microbatch_rows: int = 1):
 
 
 def _run_verifier_peer(ids, verifier, win, microbatch_rows):
-    """``run_verifier`` with the hand-off by peer stores into ``win`` (see module doc)."""
+    """``run_verifier`` with the hand-off by peer stores into ``win`` (see module doc).
+
+    With one-row microbatches on a fused CUDA stage, the add+norm kernel that
+    produces a captured residual or the final normed hidden state stores trainer r's
+    row into r's slot from its epilogue; rows produced elsewhere are copied by
+    ``peer_put`` after the stage."""
     node, stage = verifier.node, verifier.stage
     ranks = node.inference_ranks
     b, s = ids.shape
@@ -276,8 +285,8 @@ def _run_verifier_peer(ids, verifier, win, microbatch_rows):
     def owner(slot):
         return verifier.owner(caps[slot]) if slot < last_slot else ranks[-1]
 
-    # This trainer's slots of the previous step are no longer read (its kernels are
-    # ordered before this signal on the stream): their producers may store again.
+    # The previous step's slot set is no longer read by this trainer (its kernels are
+    # ordered before this signal on the stream).
     if node.training and seq > 1:
         for p in sorted({owner(i) for i in range(last_slot + 1)} - {node.rank}):
             C.peer_signal_to(win.id, 0, win.FREE, p, seq - 1)
@@ -285,7 +294,11 @@ def _run_verifier_peer(ids, verifier, win, microbatch_rows):
     if stage is not None:
         idx = ranks.index(node.rank)
         last_stage = idx == len(ranks) - 1
-        released = set()  # trainers whose previous-step slots this rank may overwrite
+        mine = [i for i in range(last_slot + 1) if owner(i) == node.rank]
+        dests = [r for r in range(min(b, ntrain)) if r != node.rank] if mine else []
+        if seq > 2:
+            for r in dests:  # r no longer reads the set of step seq - 2
+                C.peer_wait_from(win.id, 0, win.FREE, r, seq - 2, win.poll_limit)
         pending = []
         for r0 in range(0, b, microbatch_rows):
             r1 = min(b, r0 + microbatch_rows)
@@ -294,23 +307,26 @@ def _run_verifier_peer(ids, verifier, win, microbatch_rows):
             else:
                 x = torch.empty(r1 - r0, s, width, device=node.device, dtype=torch.bfloat16)
                 dist.recv(x, src=ranks[idx - 1])
-            out, captured = stage_forward(stage, x, capture=caps)
+            targets = {}
+            if r1 - r0 == 1 and r0 < ntrain and r0 != node.rank:
+                for i in mine:
+                    key = caps[i] if i < last_slot else "final"
+                    targets[key] = (win.id, r0, win.offset(i, seq))
+            stored = dict(targets)
+            out, captured = stage_forward(stage, x, capture=caps, handoff=targets)
             rows_of = [(i, captured[caps[i]]) for i in range(last_slot) if caps[i] in captured]
             if last_stage:
                 rows_of.append((last_slot, out))
             for i, h in rows_of:
+                key = caps[i] if i < last_slot else "final"
                 for row in range(r0, min(r1, ntrain)):
                     piece = h[row - r0:row - r0 + 1]
                     if row == node.rank:
                         local[i] = piece
                         continue
-                    if seq > 1 and row not in released:
-                        # wait (on the device, after this step's compute was queued, so
-                        # the verifier overlaps the trainer's previous step) until
-                        # trainer `row` released the slots of the previous step
-                        C.peer_wait_from(win.id, 0, win.FREE, row, seq - 1, win.poll_limit)
-                        released.add(row)
-                    win.put(row, i, piece)
+                    if row != r0 or key in targets or key not in stored:
+                        win.put(row, i, piece, seq)  # not stored by the producing kernel
+                    win.signal(row, i, seq)
             if not last_stage:
                 pending.append(dist.isend(out.contiguous(), ranks[idx + 1]))
         for w in pending:
@@ -322,6 +338,6 @@ def _run_verifier_peer(ids, verifier, win, microbatch_rows):
                 got.append(local[i])
             else:
                 C.peer_wait_from(win.id, 0, win.DATA + i, owner(i), seq, win.poll_limit)
-                got.append(win.view(i))
+                got.append(win.view(i, seq))
         return TeacherBatch(got[:last_slot], got[last_slot], None), ids[node.rank:node.rank + 1]
     return None, ids

@@ -299,9 +299,12 @@ def test_fused_kernels_four_ranks():
     run_ranks(4, _fused_kernels)
 
 
-def _handoff(rank, world, ckpt_path, train_gpus):
-    """Peer-store hand-off of the split layout over three steps (the slot release and
-    reuse protocol): every trainer row equals the whole verifier run on that GPU."""
+def _handoff(rank, world, ckpt_path, train_gpus, fused=False):
+    """Peer-store hand-off of the split layout over three steps (both slot sets and
+    the release protocol): every trainer row equals the whole verifier run on that
+    GPU. ``fused``: the stages run the fused FP8 path, whose add+norm epilogues store
+    the captured residuals and the final normed hidden state into the trainers'
+    slots."""
     from nanospec_b200.config import Topology
     from nanospec_b200.models.verifier import Checkpoint, QwenStage, stage_forward
     from nanospec_b200.ops._ext import cuda_ops
@@ -309,6 +312,8 @@ def _handoff(rank, world, ckpt_path, train_gpus):
     node = N.Node(train_gpus, topology=Topology(world=world, train_gpus=train_gpus))
     capture = (1, 3)
     teacher = Teacher(node, ckpt_path, capture)
+    if teacher.stage is not None:
+        assert teacher.stage.fused == fused
     full = QwenStage(Checkpoint(ckpt_path), 0, 4, device=node.device, first=True, last=True) if node.training else None
     for step in range(3):
         ids = torch.randint(0, 512, (train_gpus, 40), generator=torch.Generator().manual_seed(3 + step)).to(node.device)
@@ -326,11 +331,17 @@ def _handoff(rank, world, ckpt_path, train_gpus):
 
 
 @two_gpus
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("train_gpus", [1, 2])
-def test_verifier_handoff_by_peer_stores(train_gpus):
+def test_verifier_handoff_by_peer_stores(train_gpus, fused):
     from nanospec_b200.models.verifier import tiny_hybrid_text_config, write_synthetic_checkpoint
     with tempfile.TemporaryDirectory() as d:
-        cfg = tiny_hybrid_text_config()
-        cfg["head_dim"] = 32  # the tcgen05 verifier attention takes head dims 32..256
-        path = write_synthetic_checkpoint(os.path.join(d, "ck"), cfg, fp8=False, seed=2)
-        run_ranks(2, _handoff, str(path), train_gpus)
+        if fused:  # the 27B head geometry at small width: FP8 projections, d_v = 128
+            cfg = tiny_hybrid_text_config(hidden=256, vocab=512, heads=2, head_dim=128, ffn=512)
+            cfg.update(linear_num_key_heads=1, linear_num_value_heads=2, linear_key_head_dim=128,
+                       linear_value_head_dim=128, num_key_value_heads=1)
+        else:
+            cfg = tiny_hybrid_text_config()
+            cfg["head_dim"] = 32  # the tcgen05 verifier attention takes head dims 32..256
+        path = write_synthetic_checkpoint(os.path.join(d, "ck"), cfg, fp8=fused, seed=2)
+        run_ranks(2, _handoff, str(path), train_gpus, fused)
