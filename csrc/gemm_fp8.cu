@@ -182,11 +182,13 @@ __global__ void __launch_bounds__(F8Cfg<BN>::THREADS, 1)
       for (int j = 0; j < CPW; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int buf = it & 1;
+        // the block scales do not depend on the MMA: load them before the wait so
+        // their latency hides behind it
+        const float sbv = args.sb[nb * kbs + kb];
+        const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + kb] : 0.f;
         ok = sm100::mbar_wait(&tfull[buf], (it >> 1) & 1, args.err);
         if (!ok) break;
         sm100::tc_fence_after();
-        const float sbv = args.sb[nb * kbs + kb];
-        const float sav = (m < args.M) ? args.sa[(int64_t)m * kbs + kb] : 0.f;
         const float f = sav * sbv;
 #pragma unroll
         for (int c = 0; c < CPW; c += 32) {
