@@ -666,6 +666,15 @@ __global__ void __launch_bounds__(192, 1)
     const int r = qw * 32 + lane;  // value channel = TMEM lane = A-operand row
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     bool ok = true;
+    float un[C];  // U^T row r of the next chunk
+    if (nchunks > 0) {
+      const float4* up = reinterpret_cast<const float4*>(Ut + (ck0 * 128 + r) * C);
+#pragma unroll
+      for (int j = 0; j < C / 4; ++j) {
+        const float4 t = up[j];
+        un[4 * j] = t.x, un[4 * j + 1] = t.y, un[4 * j + 2] = t.z, un[4 * j + 3] = t.w;
+      }
+    }
     for (int ch = 0; ch < nchunks && ok; ++ch) {
       const int64_t ck = ck0 + ch;
       // ---- (a) state operand for this chunk
@@ -675,6 +684,7 @@ __global__ void __launch_bounds__(192, 1)
           *reinterpret_cast<uint4*>(sS + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
               make_uint4(0u, 0u, 0u, 0u);
       } else {
+        const float gl = GL[ck];  // independent of the MMAs: load before the wait
         ok = __all_sync(0xffffffff, sm100::mbar_wait(mm34, (ch - 1) & 1, err));
         if (!ok) break;
         sm100::tc_fence_after();
@@ -686,11 +696,11 @@ __global__ void __launch_bounds__(192, 1)
           for (int c = 0; c < C; c += 32) {
             float o[32];
             sm100::tmem_ld32(tmem + lane_off + O_COL + c, o);
-            for (int i = 0; i < 32 && c + i < cnt; ++i)
-              out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)  // constant indices: o stays in registers
+              if (c + i < cnt) out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
           }
         }
-        const float gl = GL[ck];
 #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
           float v[32];
@@ -710,21 +720,24 @@ __global__ void __launch_bounds__(192, 1)
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(a_ready);
-      // ---- (b) v^T = U^T - S^T W^T
+      // ---- (b) v^T = U^T - S^T W^T; U of the next chunk is loaded now (it is used
+      //      one chunk later, so its latency hides behind this chunk's MMAs)
       float u[C];
-      {
-        const float4* up = reinterpret_cast<const float4*>(Ut + (ck * 128 + r) * C);
+#pragma unroll
+      for (int j = 0; j < C; ++j) u[j] = un[j];
+      if (ch + 1 < nchunks) {
+        const float4* up = reinterpret_cast<const float4*>(Ut + ((ck + 1) * 128 + r) * C);
 #pragma unroll
         for (int j = 0; j < C / 4; ++j) {
           const float4 t = up[j];
-          u[4 * j] = t.x, u[4 * j + 1] = t.y, u[4 * j + 2] = t.z, u[4 * j + 3] = t.w;
+          un[4 * j] = t.x, un[4 * j + 1] = t.y, un[4 * j + 2] = t.z, un[4 * j + 3] = t.w;
         }
       }
       ok = __all_sync(0xffffffff, sm100::mbar_wait(mm12, ch & 1, err));
       if (!ok) break;
       sm100::tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < C; c += 32) {
+#pragma unroll
+      for (int c = 0; c < C; c += 32) {  // fully unrolled: u stays in registers
         float v[32];
         sm100::tmem_ld32(tmem + lane_off + VN_COL + c, v);
 #pragma unroll
@@ -751,8 +764,9 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < C; c += 32) {
           float o[32];
           sm100::tmem_ld32(tmem + lane_off + O_COL + c, o);
-          for (int i = 0; i < 32 && c + i < cnt; ++i)
-            out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)  // constant indices: o stays in registers
+            if (c + i < cnt) out[(((int64_t)bi * s + t0 + c + i) * nv + h) * 128 + r] = __float2bfloat16(o[i]);
         }
       }
     }
